@@ -1,0 +1,327 @@
+"""Benchmark of the B200 multivector-product hot path.
+
+Headline (BASELINE.json metric): Cl(8,0) geom_prod forward + backward,
+multivector products/s, with the per-GPU batch of config 3's global batch
+split over 8 GPUs (524,288 products of 256 blades per GPU, weak scaling).
+One step = forward sum + both backward sums over the GPU's batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line. `value` is measured on device-resident inputs
+(CUDA events, max over ranks); `e2e` is the same metric through the public
+API with host (pinned) buffers, copies inside the timed region. The
+reference arm (`--impl reference`) times the reference's CPU algorithm (the
+oracle's torch port of _shared/_einsum_refs.py) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_GEN = 8
+D = 1 << N_GEN
+PER_GPU_BATCH = 4_194_304 // 8       # config 3's global batch over 8 GPUs
+METRIC = "Cl(8,0) geom_prod fwd+bwd multivector products/s at 1/8 B200; % of FP32 peak"
+UNIT = "products/s"
+NNZ_GP = 4 ** N_GEN                   # non-zeros of the Cl(8,0) sign table
+FLOPS_PER_SUM = 2 * NNZ_GP            # one FMA per non-zero term
+BYTES_PER_SUM = 3 * D * 4             # two operand rows read, one row written
+# DRAM bytes per row of one bilinear_tiled_kernel launch, from ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum / rows). None until captured.
+MEASURED_TRAFFIC_PER_SUM = None
+
+
+def _env_int(k, d):
+    return int(os.environ.get(k, d))
+
+
+def fp32_peak_tflops(device):
+    """Nominal FP32 CUDA-core peak at max SM clock: SMs x 128 FMA/clk x 2."""
+    props = torch.cuda.get_device_properties(device)
+    mhz = 1965.0
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f).get("sm_max_mhz", mhz))
+    except Exception:
+        pass
+    return props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML (read-only) every
+    200 ms while the timed region runs."""
+
+    REASONS = {
+        "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self.h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: reported as unsampled
+            self.err = repr(e)
+            self.h = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        if self.h is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.h is not None:
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_port_rate(rows, threads, seed=0):
+    """Products/s of the oracle's torch port of the reference CPU path
+    (outer product x signs, scatter-add; autograd backward) in fp32."""
+    from oracle.ga_oracle import EinsumProduct
+    torch.set_num_threads(threads)
+    f = EinsumProduct("gp", N_GEN, (1,) * N_GEN, dtype=torch.float32)
+    gen = torch.Generator().manual_seed(seed)
+    chunk = 256
+
+    def one_pass(nrows):
+        a = torch.randn(nrows, D, generator=gen, requires_grad=True)
+        b = torch.randn(nrows, D, generator=gen, requires_grad=True)
+        g = torch.randn(nrows, D, generator=gen)
+        t0 = time.perf_counter()
+        for s in range(0, nrows, chunk):
+            c = f(a[s:s + chunk], b[s:s + chunk])
+            c.backward(g[s:s + chunk])
+        return time.perf_counter() - t0
+
+    one_pass(chunk)                       # warm-up
+    return rows / one_pass(rows)
+
+
+def workload_config(n_gpus):
+    return {"workload": "Cl(8,0) geom_prod fwd+bwd (batch-by-batch), 524288 products of "
+                        "256 fp32 blades per GPU (config 3 global batch / 8), N(0,1)",
+            "per_gpu_batch": PER_GPU_BATCH, "global_batch": PER_GPU_BATCH * n_gpus,
+            "dim": D, "metric": [1] * N_GEN,
+            "parallelism": f"dp{n_gpus} (row shards, no collective)",
+            "l2": "inputs 1.5 GB per GPU > 126 MB L2; no flush needed"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    rows = 1024
+    for _ in range(args.warmup):
+        cpu_port_rate(256, threads)
+    rates = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        rates.append(cpu_port_rate(rows, threads))
+    elapsed = time.perf_counter() - t0
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} Cl(8,0) products fwd+bwd per step, fp32 torch "
+                                   f"einsum port of _shared/_einsum_refs.py"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local = _env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import cliffordcuda_b200 as cc
+    from cliffordcuda_b200 import _lib
+    from cliffordcuda_b200.products import bilinear_raw
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    metric = (1,) * N_GEN
+    B = PER_GPU_BATCH
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    a = torch.randn(B, D, device=dev, generator=gen)
+    b = torch.randn(B, D, device=dev, generator=gen)
+    g = torch.randn(B, D, device=dev, generator=gen)
+    c = torch.empty_like(a)
+    ga = torch.empty_like(a)
+    gb = torch.empty_like(a)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(events=None):
+        calls = (("fwd", a, b, c), ("grad_a", b, g, ga), ("grad_b", a, g, gb))
+        for i, (mode, x, y, o) in enumerate(calls):
+            if events is not None:
+                events[i][0].record(stream)
+            bilinear_raw("gp", mode, x, y, N_GEN, metric, out=o)
+            if events is not None:
+                events[i][1].record(stream)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    _lib.device_status(dev)
+
+    K = args.steps
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(3)]
+          for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev) as clk:
+        t_start.record(stream)
+        for k in range(K):
+            step(ev[k])
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = t_start.elapsed_time(t_end)
+    launch_ms = [e[0].elapsed_time(e[1]) for s in ev for e in s]
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    _lib.device_status(dev)
+    value = world * B * K / (ms / 1000.0)
+    kernel_ms = statistics.mean(launch_ms)
+    achieved = FLOPS_PER_SUM * B / (kernel_ms / 1000.0) / 1e12
+    peak = fp32_peak_tflops(dev)
+
+    # ---- end to end through the public API, host (pinned) buffers
+    ha = a.cpu().pin_memory()
+    hb = b.cpu().pin_memory()
+    hg = g.cpu().pin_memory()
+    hc, hga, hgb = (torch.empty_like(ha).pin_memory() for _ in range(3))
+
+    def e2e_step():
+        da = ha.to(dev, non_blocking=True).requires_grad_(True)
+        db = hb.to(dev, non_blocking=True).requires_grad_(True)
+        dg = hg.to(dev, non_blocking=True)
+        out = cc.geom_prod(da, db, metric=metric)
+        out.backward(dg)
+        hc.copy_(out.detach(), non_blocking=True)
+        hga.copy_(da.grad, non_blocking=True)
+        hgb.copy_(db.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    K2 = max(1, min(K, 5))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K2):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+    e2e_value = world * B * K2 / (e2e_ms / 1000.0)
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            rows = 8192
+            cpu = {"value": cpu_port_rate(rows, threads), "unit": UNIT, "cores": threads,
+                   "kind": "port",
+                   "sample": f"{rows} Cl(8,0) products fwd+bwd, fp32 torch einsum port of "
+                             f"_shared/_einsum_refs.py, {threads} threads"}
+        traffic = (MEASURED_TRAFFIC_PER_SUM * B) if MEASURED_TRAFFIC_PER_SUM else None
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1), seeded per rank",
+            "config": workload_config(world),
+            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": "nominal FP32 CUDA-core peak: SMs x 128 FMA/clk x 2 "
+                                        "x sm_max_mhz of MEASURED_PEAKS.json",
+                         "kernel": "bilinear_tiled_kernel", "kernel_ms_per_launch": kernel_ms,
+                         "hbm_gbs": BYTES_PER_SUM * B / (kernel_ms / 1000.0) / 1e9},
+            "pct_fp32_peak": 100.0 * achieved / peak,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 3 * B * D * 4,
+                    "d2h_bytes_per_step": 3 * B * D * 4,
+                    "path": "cliffordcuda_b200.geom_prod + autograd backward, pinned host "
+                            "buffers, copies inside the timed region"},
+            "gpu_launches": 3 * K,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

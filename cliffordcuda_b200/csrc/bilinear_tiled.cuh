@@ -1,0 +1,398 @@
+// bilinear_tiled.cuh -- the tiled batch-by-batch bilinear kernel (fp32 FFMA
+// on the CUDA cores), instantiated per sum in bilinear_tiled_{fwd,ga,gb}.cu.
+//
+// Every product of the reference (geometric, wedge, inner, left/right
+// contraction) and both of its backward sums have the form
+//
+//     out[k] = sum_i  s(P, Q) * x[i] * y[i ^ k]
+//
+// with (P, Q) = (i, i^k) for the forward sum, (k, i) for grad_a and (i, k)
+// for grad_b, and s = (blade sign of e_P e_Q) x (product predicate on P, Q)
+// (reference: extensions/ga/geom_prod.py:216-250 -- the forward LUT and the
+// two transposed backward LUTs -- and the masks of _shared/_einsum_refs.py).
+//
+// Blade indices split into a high part (bits 4..n-1) and a low part (bits
+// 0..3). The sign factorises as
+//     s(P, Q) = s_H(P_h, Q_h) * s_L(P_l, Q_l) * (-1)^(popc(P_h) * popc(Q_l))
+// (every high generator of P passes every low generator of Q; none of the
+// reverse pairs reorder), and every product predicate except the inner
+// product's factorises the same way. The kernel therefore works on 16 x 16
+// register blocks: a thread owns the 16 outputs of one high block k_h of one
+// row and sweeps the high blocks i_h, each step doing up to 256 FFMAs of
+//     acc[k_l] += c(i_l, k_l) * x[i_h, i_l] * y'[i_h ^ k_h, i_l ^ k_l]
+// whose coefficients c in {-1, 0, +1} are compile-time constants (this needs
+// the low four generators to square to +1; other metrics take the generic
+// kernel). The runtime high-part sign and predicate are folded into y' (16
+// FMULs per step, read from a per-CTA table); the (-1)^(popc * popc) cross
+// term is either a compile-time body variant chosen by the warp-uniform
+// parity of i_h (forward, grad_b) or a per-lane sign on y' plus a sign on the
+// outputs (grad_a).
+//
+// Data movement: persistent CTAs of 256 threads; a tile is 4096 floats of x
+// and of y (4096 / 2^n rows), brought in by 2-D TMA loads with 128-byte
+// swizzle into a two-stage mbarrier pipeline; results leave through a
+// swizzled shared tile and a TMA store. The swizzle makes the XOR-indexed
+// 64-byte block reads of y conflict-free in shared memory.
+//
+// The inner product's predicate (P subset Q or Q subset P) does not factor;
+// it is evaluated as left + right contraction minus the doubly counted
+// P == Q terms.
+#pragma once
+#include <algorithm>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace cb {
+namespace tiled {
+
+constexpr int kThreads = 256;
+constexpr int kBlk = 16;                      // low block: 4 generators
+constexpr int kTileFloats = kThreads * kBlk;  // 4096 floats per operand tile
+constexpr int kTileLines = kTileFloats / 32;  // 128 lines of 128 bytes
+constexpr int kTileBytes = kTileFloats * 4;
+
+enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4 };
+
+__host__ __device__ constexpr int popc4(int v) {
+    return (v & 1) + ((v >> 1) & 1) + ((v >> 2) & 1) + ((v >> 3) & 1);
+}
+
+__host__ __device__ constexpr int reorder4(int p, int q) {
+    int c = 0;
+    for (int a = 0; a < 4; ++a)
+        if ((p >> a) & 1)
+            for (int b = 0; b < a; ++b) c += (q >> b) & 1;
+    return c & 1;
+}
+
+// Coefficient of x[i_l] * y[i_l ^ k_l] in output k_l for the low block.
+template <int MODE, int OPK, int PAR>
+__host__ __device__ constexpr int low_coef(int il, int kl) {
+    const int jl = il ^ kl;
+    const int P = (MODE == CB_MODE_GRAD_A) ? kl : il;
+    const int Q = (MODE == CB_MODE_FWD) ? jl : (MODE == CB_MODE_GRAD_A ? il : kl);
+    const bool m = (OPK == OPK_GP)      ? true
+                   : (OPK == OPK_WEDGE) ? ((P & Q) == 0)
+                   : (OPK == OPK_LC)    ? ((P & ~Q & 15) == 0)
+                                        : ((Q & ~P & 15) == 0);
+    if (!m) return 0;
+    int s = reorder4(P, Q);
+    if (PAR) {
+        if (MODE == CB_MODE_FWD) s ^= popc4(jl) & 1;
+        if (MODE == CB_MODE_GRAD_B) s ^= popc4(kl) & 1;
+    }
+    return s ? -1 : 1;
+}
+
+template <int MODE, int OPK, int PAR>
+__device__ __forceinline__ void block_fma(float (&acc)[kBlk], const float (&xv)[kBlk],
+                                          const float (&yv)[kBlk]) {
+#pragma unroll
+    for (int il = 0; il < kBlk; ++il)
+#pragma unroll
+        for (int kl = 0; kl < kBlk; ++kl) {
+            const int c = low_coef<MODE, OPK, PAR>(il, kl);
+            if (c > 0) acc[kl] = fmaf(xv[il], yv[il ^ kl], acc[kl]);
+            if (c < 0) acc[kl] = fmaf(-xv[il], yv[il ^ kl], acc[kl]);
+        }
+}
+
+// Swizzled shared tile: float f of the tile lives in 128-byte line f >> 5, in
+// 16-byte chunk ((f >> 2) & 7) ^ (line & 7) -- the TMA 128B swizzle pattern.
+__device__ __forceinline__ void load_block(const float *tile, int f0, float (&v)[kBlk]) {
+    const int line = f0 >> 5;
+    const int c0 = (f0 >> 2) & 7;
+    const float *lp = tile + line * 32;
+    const int sw = line & 7;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const float4 q = *reinterpret_cast<const float4 *>(lp + (((c0 + t) ^ sw) << 2));
+        v[4 * t + 0] = q.x;
+        v[4 * t + 1] = q.y;
+        v[4 * t + 2] = q.z;
+        v[4 * t + 3] = q.w;
+    }
+}
+
+__device__ __forceinline__ void store_block(float *tile, int f0, const float (&v)[kBlk]) {
+    const int line = f0 >> 5;
+    const int c0 = (f0 >> 2) & 7;
+    float *lp = tile + line * 32;
+    const int sw = line & 7;
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+        *reinterpret_cast<float4 *>(lp + (((c0 + t) ^ sw) << 2)) =
+            make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+}
+
+__device__ __forceinline__ int swz_index(int f) {
+    const int line = f >> 5;
+    return line * 32 + ((((f >> 2) & 7) ^ (line & 7)) << 2) + (f & 3);
+}
+
+__device__ __forceinline__ void apply_sign(float (&yv)[kBlk], float2 sg) {
+#pragma unroll
+    for (int e = 0; e < kBlk; ++e) yv[e] *= (popc4(e) & 1) ? sg.y : sg.x;
+}
+
+// High-part factor of the step (i_h, k_h) for one predicate: the blade sign
+// of the high parts times the high-part predicate; .y adds grad_a's per-lane
+// (-1)^popc(k_h) for odd-parity y elements.
+__device__ __forceinline__ float2 high_factor(int mode, int opk, uint32_t ih, uint32_t kh,
+                                              uint32_t negH, uint32_t zeroH) {
+    const uint32_t jh = ih ^ kh;
+    const uint32_t P = (mode == CB_MODE_GRAD_A) ? kh : ih;
+    const uint32_t Q = (mode == CB_MODE_FWD) ? jh : (mode == CB_MODE_GRAD_A ? ih : kh);
+    bool m = true;
+    if (opk == OPK_WEDGE) m = (P & Q) == 0;
+    if (opk == OPK_LC) m = (P & ~Q) == 0;
+    if (opk == OPK_RC) m = (Q & ~P) == 0;
+    const float s = m ? (float)blade_sign(P, Q, negH, zeroH) : 0.0f;
+    const float so = (mode == CB_MODE_GRAD_A && parity(kh)) ? -s : s;
+    return make_float2(s, so);
+}
+
+__host__ __device__ inline size_t table_entries(int n, bool inner) {
+    const size_t nh = size_t(1) << (n - 4);
+    return nh * nh * (inner ? 2 : 1);
+}
+
+__host__ __device__ inline size_t smem_bytes(int n, bool inner) {
+    return 1024 /* alignment slack */ + 5 * size_t(kTileBytes) +
+           table_entries(n, inner) * sizeof(float2) + kThreads * sizeof(float) + 64;
+}
+
+template <int MODE, int OPK>
+__device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const float *yt,
+                                      const float2 *tab, const float2 *tab2, int rowf, int kh,
+                                      int lgNH) {
+    const int NH = 1 << lgNH;
+    // Even-parity i_h first, then odd: the parity-dependent body variant is
+    // fixed within each loop (t -> 2t | parity(t) enumerates the even ones,
+    // 2t | !parity(t) the odd ones).
+#pragma unroll 1
+    for (int par = 0; par < 2; ++par) {
+#pragma unroll 1
+        for (int t = 0; t < (NH >> 1); ++t) {
+            const int ih = (t << 1) | (parity(t) ^ par);
+            const int jh = ih ^ kh;
+            float xv[kBlk], yv[kBlk];
+            load_block(xt, rowf + ih * kBlk, xv);
+            load_block(yt, rowf + jh * kBlk, yv);
+            const float2 sg = tab[(ih << lgNH) | kh];
+            const bool odd = (MODE != CB_MODE_GRAD_A) && par;
+            if (OPK == OPK_INNER) {
+                const float2 sg2 = tab2[(ih << lgNH) | kh];
+                float y2[kBlk];
+#pragma unroll
+                for (int e = 0; e < kBlk; ++e) y2[e] = yv[e];
+                apply_sign(yv, sg);
+                apply_sign(y2, sg2);
+                if (odd) {
+                    block_fma<MODE, OPK_LC, 1>(acc, xv, yv);
+                    block_fma<MODE, OPK_RC, 1>(acc, xv, y2);
+                } else {
+                    block_fma<MODE, OPK_LC, 0>(acc, xv, yv);
+                    block_fma<MODE, OPK_RC, 0>(acc, xv, y2);
+                }
+            } else {
+                apply_sign(yv, sg);
+                if (odd)
+                    block_fma<MODE, OPK, 1>(acc, xv, yv);
+                else
+                    block_fma<MODE, OPK, 0>(acc, xv, yv);
+            }
+        }
+    }
+}
+
+template <int MODE, int OPK>
+__global__ void __launch_bounds__(kThreads)
+    bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
+                          const __grid_constant__ CUtensorMap my,
+                          const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
+                          uint32_t zero, int num_tiles, int *err) {
+    extern __shared__ unsigned char smem_raw[];
+    const uintptr_t base =
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
+    float *xs = reinterpret_cast<float *>(base);  // [2][kTileFloats]
+    float *ys = xs + 2 * kTileFloats;             // [2][kTileFloats]
+    float *os = ys + 2 * kTileFloats;             // [kTileFloats]
+    const int lgNH = n - 4;
+    const int NH = 1 << lgNH;
+    constexpr bool inner = (OPK == OPK_INNER);
+    float2 *tab = reinterpret_cast<float2 *>(os + kTileFloats);
+    float2 *tab2 = tab + NH * NH;
+    float *diag = reinterpret_cast<float *>(tab + table_entries(n, inner));
+    uint64_t *full = reinterpret_cast<uint64_t *>(diag + kThreads);
+
+    const int tid = threadIdx.x;
+    const int D = 1 << n;
+    const int r = tid >> lgNH;
+    const int kh = tid & (NH - 1);
+    const int rowf = r * D;
+    const uint32_t negH = neg >> 4, zeroH = zero >> 4;
+
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_barrier_init();
+        prefetch_tensormap(&mx);
+        prefetch_tensormap(&my);
+        prefetch_tensormap(&mo);
+    }
+    // per-CTA table of high-part factors, [i_h][k_h]
+    for (int e = tid; e < NH * NH; e += kThreads) {
+        const uint32_t ih = e >> lgNH, k = e & (NH - 1);
+        if (inner) {
+            tab[e] = high_factor(MODE, OPK_LC, ih, k, negH, zeroH);
+            tab2[e] = high_factor(MODE, OPK_RC, ih, k, negH, zeroH);
+        } else {
+            tab[e] = high_factor(MODE, OPK, ih, k, negH, zeroH);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int s = 0; s < 2; ++s) {
+            const int tile = blockIdx.x + s * gridDim.x;
+            if (tile < num_tiles) {
+                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
+                tma_load_2d(xs + s * kTileFloats, &mx, 0, tile * kTileLines, &full[s]);
+                tma_load_2d(ys + s * kTileFloats, &my, 0, tile * kTileLines, &full[s]);
+            }
+        }
+    }
+
+    for (int it = 0;; ++it) {
+        const int tile = blockIdx.x + it * gridDim.x;
+        if (tile >= num_tiles) break;
+        const int s = it & 1;
+        if (!mbar_wait_bounded(&full[s], (it >> 1) & 1, err, 0x101)) break;
+        const float *xt = xs + s * kTileFloats;
+        const float *yt = ys + s * kTileFloats;
+
+        float acc[kBlk];
+#pragma unroll
+        for (int e = 0; e < kBlk; ++e) acc[e] = 0.0f;
+        sweep<MODE, OPK>(acc, xt, yt, tab, tab2, rowf, kh, lgNH);
+
+        if (MODE == CB_MODE_GRAD_A && parity(kh)) {
+#pragma unroll
+            for (int e = 0; e < kBlk; ++e)
+                if (popc4(e) & 1) acc[e] = -acc[e];
+        }
+        // inner: remove the P == Q terms counted by both contractions.
+        // s(k, k) = s_H(k_h, k_h) s_L(k_l, k_l) (-1)^(popc(k_h) popc(k_l)).
+        float dpart = 0.0f;
+        if (inner) {
+            float xv[kBlk];
+            load_block(xt, rowf + kh * kBlk, xv);
+            const int shh = blade_sign(kh, kh, negH, zeroH);
+            if (MODE == CB_MODE_FWD) {  // out[0] -= sum_i s(i, i) x_i y_i
+                float yv[kBlk];
+                load_block(yt, rowf + kh * kBlk, yv);
+#pragma unroll
+                for (int e = 0; e < kBlk; ++e) {
+                    const int sl = (reorder4(e, e) ^ ((popc4(e) & 1) & parity(kh))) ? -1 : 1;
+                    dpart = fmaf((float)(shh * sl) * xv[e], yv[e], dpart);
+                }
+            } else {  // out[k] -= s(k, k) x_k y_0
+                const float y0 = yt[swz_index(rowf)];
+#pragma unroll
+                for (int e = 0; e < kBlk; ++e) {
+                    const int sl = (reorder4(e, e) ^ ((popc4(e) & 1) & parity(kh))) ? -1 : 1;
+                    acc[e] = fmaf(-(float)(shh * sl) * xv[e], y0, acc[e]);
+                }
+            }
+        }
+
+        if (tid == 0) bulk_wait_read_all();  // previous tile's store has left `os`
+        __syncthreads();                     // stage s consumed by every thread
+        if (tid == 0) {
+            const int next = tile + 2 * gridDim.x;
+            if (next < num_tiles) {
+                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
+                tma_load_2d(xs + s * kTileFloats, &mx, 0, next * kTileLines, &full[s]);
+                tma_load_2d(ys + s * kTileFloats, &my, 0, next * kTileLines, &full[s]);
+            }
+        }
+        store_block(os, rowf + kh * kBlk, acc);
+        if (inner && MODE == CB_MODE_FWD) diag[tid] = dpart;
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (inner && MODE == CB_MODE_FWD) {
+            if (tid < (kThreads >> lgNH)) {
+                float sum = 0.0f;
+                for (int q = 0; q < NH; ++q) sum += diag[(tid << lgNH) + q];
+                os[swz_index(tid * D)] -= sum;
+                fence_proxy_async_smem();
+            }
+            __syncthreads();
+        }
+        if (tid == 0) {
+            tma_store_2d(&mo, os, 0, tile * kTileLines);
+            bulk_commit();
+        }
+    }
+    if (tid == 0) bulk_wait_all();
+}
+
+template <int MODE, int OPK>
+int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int n, uint32_t neg,
+                 uint32_t zero, cudaStream_t stream) {
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    int *err = nullptr;
+    if ((st = device_error_word(&err))) return st;
+    const int D = 1 << n;
+    const uint64_t lines = (uint64_t)batch * D / 32;
+    CUtensorMap mx, my, mo;
+    if ((st = make_tmap_lines(&mx, x, lines, kTileLines))) return st;
+    if ((st = make_tmap_lines(&my, y, lines, kTileLines))) return st;
+    if ((st = make_tmap_lines(&mo, out, lines, kTileLines))) return st;
+    const size_t smem = smem_bytes(n, OPK == OPK_INNER);
+    auto kern = bilinear_tiled_kernel<MODE, OPK>;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bilinear_tiled)");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (per_sm < 1) {
+        set_error("bilinear tiled kernel does not fit an SM (smem %zu)", smem);
+        return CB_ERR_UNSUPPORTED;
+    }
+    const int rows_per_tile = kTileFloats / D;
+    const int64_t tiles = (batch + rows_per_tile - 1) / rows_per_tile;
+    if (tiles > ((int64_t)1 << 30)) {
+        set_error("batch too large for one call");
+        return CB_ERR_UNSUPPORTED;
+    }
+    const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * di.sm_count);
+    kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch bilinear_tiled_kernel");
+    return CB_OK;
+}
+
+}  // namespace tiled
+
+// Explicitly instantiated per mode in bilinear_tiled_{fwd,ga,gb}.cu.
+template <int MODE>
+int bilinear_tiled(int op, const float *x, const float *y, float *out, int64_t batch, int n,
+                   uint32_t neg, uint32_t zero, cudaStream_t stream) {
+    using namespace tiled;
+    switch (op) {
+    case CB_OP_GP: return launch_tiled<MODE, OPK_GP>(x, y, out, batch, n, neg, zero, stream);
+    case CB_OP_WEDGE: return launch_tiled<MODE, OPK_WEDGE>(x, y, out, batch, n, neg, zero, stream);
+    case CB_OP_LC: return launch_tiled<MODE, OPK_LC>(x, y, out, batch, n, neg, zero, stream);
+    case CB_OP_RC: return launch_tiled<MODE, OPK_RC>(x, y, out, batch, n, neg, zero, stream);
+    case CB_OP_INNER: return launch_tiled<MODE, OPK_INNER>(x, y, out, batch, n, neg, zero, stream);
+    }
+    set_error("op %d has no tiled kernel", op);
+    return CB_ERR_INVALID;
+}
+
+}  // namespace cb

@@ -1,0 +1,159 @@
+// common.cuh -- shared device helpers for the cliffordcuda_b200 kernels:
+// blade sign arithmetic, mbarrier / TMA (cp.async.bulk.tensor) wrappers and
+// the library-wide error state.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/cliffordcuda_b200.h"
+
+namespace cb {
+
+// ------------------------------------------------------------ error state --
+// Host side: thread-local message returned by cb_last_error().
+void set_error(const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);
+
+// Device side: the first failing kernel records a code in the library's
+// device error word (bounded waits that ran out; never a trap). Kernels get
+// its address as an argument; cb_device_status() reads and clears it.
+int device_error_word(int **out);  // address for the current device; cached
+
+// ------------------------------------------------------------ blade signs --
+// Bit b of suffix_parity(p) is the parity of popcount(p >> (b + 1)): the
+// number of generators of blade p that a generator b has to move past.
+__host__ __device__ __forceinline__ uint32_t suffix_parity(uint32_t p) {
+    uint32_t s = p >> 1;
+    s ^= s >> 1;
+    s ^= s >> 2;
+    s ^= s >> 4;
+    s ^= s >> 8;
+    s ^= s >> 16;
+    return s;
+}
+
+__host__ __device__ __forceinline__ int parity(uint32_t v) {
+#ifdef __CUDA_ARCH__
+    return __popc(v) & 1;
+#else
+    return __builtin_popcount(v) & 1;
+#endif
+}
+
+// Reordering sign of e_p e_q: (-1)^#{(a, b): a > b, a in p, b in q}.
+__host__ __device__ __forceinline__ int reorder_parity(uint32_t p, uint32_t q) {
+    return parity(q & suffix_parity(p));
+}
+
+// Full geometric-product sign of e_p e_q under the metric given as two masks
+// (generators squaring to -1 and to 0): +1, -1 or 0.
+__host__ __device__ __forceinline__ int blade_sign(uint32_t p, uint32_t q, uint32_t neg,
+                                                   uint32_t zero) {
+    uint32_t c = p & q;
+    if (c & zero) return 0;
+    return (reorder_parity(p, q) ^ parity(c & neg)) ? -1 : 1;
+}
+
+// Product predicate on the blade pair (p, q) (the pair the sign is taken on).
+__host__ __device__ __forceinline__ bool op_mask(int op, uint32_t p, uint32_t q) {
+    switch (op) {
+    case CB_OP_GP: return true;
+    case CB_OP_WEDGE: return (p & q) == 0;
+    case CB_OP_INNER: return ((p & ~q) == 0) || ((q & ~p) == 0);
+    case CB_OP_LC: return (p & ~q) == 0;
+    case CB_OP_RC: return (q & ~p) == 0;
+    default: return false;
+    }
+}
+
+// ------------------------------------------------------- PTX: mbarrier/TMA --
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after `limit` polls, records `code` in the device
+// error word and returns false. try_wait itself suspends for a
+// hardware-defined interval per poll, so the limit bounds wall time to
+// roughly a second or more.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, int *err,
+                                                  int code, uint32_t limit = (1u << 22)) {
+    for (uint32_t it = 0; it < limit; ++it)
+        if (mbar_try_wait(bar, phase)) return true;
+    atomicCAS(err, 0, code);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *smem_src, int x,
+                                             int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// --------------------------------------------------------- host utilities --
+struct DeviceInfo {
+    int sm_count = 0;
+    int max_smem_optin = 0;
+};
+int device_info(DeviceInfo *out);  // for the current device; cached
+
+// 2-D tensor map over `lines` rows of 32 fp32 (128 B), box 32 x box_lines,
+// 128-byte swizzle. Returns CB_OK or an error status.
+int make_tmap_lines(CUtensorMap *map, const void *base, uint64_t lines, uint32_t box_lines);
+
+}  // namespace cb

@@ -1,0 +1,100 @@
+/*
+ * cliffordcuda_b200.h -- C ABI of the B200 (sm_100a) multivector-product
+ * library. Plain pointers, sizes and bitmasks only; no torch types.
+ *
+ * Conventions shared by every entry point:
+ *   - multivectors are row-major (batch, 2^n) fp32 arrays in bit-pattern blade
+ *     order (blade index bit t set <=> generator e_t present);
+ *   - the metric of Cl(p, q, r) is passed as two bitmasks: bit t of `neg_mask`
+ *     set <=> e_t^2 = -1, bit t of `zero_mask` set <=> e_t^2 = 0 (all other
+ *     generators square to +1). The reference passed packed sign/validity
+ *     lookup tables instead; no table is needed here;
+ *   - every pointer is device memory of the current CUDA device, allocated by
+ *     the caller. The library never frees caller memory;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). All work is
+ *     stream-ordered and asynchronous; no entry point synchronises the host
+ *     unless its comment says so;
+ *   - return value: CB_OK (0) or an error status. cb_last_error() returns a
+ *     thread-local message for the last failure on the calling thread.
+ *
+ * Reference paths below are relative to the CliffordCUDA project root.
+ */
+#ifndef CLIFFORDCUDA_B200_H
+#define CLIFFORDCUDA_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CB_API __attribute__((visibility("default")))
+#else
+#define CB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define CB_OK 0
+#define CB_ERR_INVALID 1     /* bad argument (shape, op, mode, metric, alignment) */
+#define CB_ERR_CUDA 2        /* a CUDA runtime / driver call failed */
+#define CB_ERR_UNSUPPORTED 3 /* valid request outside what this build supports */
+#define CB_ERR_DEVICE 4      /* a kernel reported a device-side failure (bounded wait expired) */
+
+/* products */
+#define CB_OP_GP 0    /* geometric product                 extensions/ga/geom_prod.py:253      */
+#define CB_OP_WEDGE 1 /* outer product (i & j == 0)         extensions/ga/wedge_prod/chunk.py:105 */
+#define CB_OP_INNER 2 /* Hestenes inner, scalars included   extensions/ga/inner_prod/chunk.py:101 */
+#define CB_OP_LC 3    /* left contraction (i subset j)      extensions/ga/left_contract.py:121  */
+#define CB_OP_RC 4    /* right contraction (j subset i)     extensions/ga/right_contract.py:76  */
+#define CB_OP_REG 5   /* regressive (non-degenerate only)   extensions/ga/regressive_prod.py:186 */
+
+/* sums */
+#define CB_MODE_FWD 0    /* out[k] = sum_i s(i, i^k) x[i] y[i^k]; (x, y) = (a, b) */
+#define CB_MODE_GRAD_A 1 /* out[k] = sum_i s(k, i)   x[i] y[k^i]; (x, y) = (b, g) */
+#define CB_MODE_GRAD_B 2 /* out[k] = sum_i s(i, k)   x[i] y[k^i]; (x, y) = (a, g) */
+
+/*
+ * One batch-by-batch bilinear sum of product `op` (s = signed product mask).
+ * Replaces the pybind entry points geom_prod_fwd (kernels/ga/geom_prod.cu:553-571),
+ * wedge_prod_fwd (kernels/ga/wedge_prod.cu:220-224), inner_prod_fwd
+ * (kernels/ga/inner_prod.cu:298-307) and contract_fwd (kernels/ga/contract.cu:203-208),
+ * each of which the reference also called with transposed LUTs for its two
+ * backward sums (extensions/ga/geom_prod.py:241-250). For CB_OP_REG it
+ * replaces the geom_prod_fwd + index_select pair of regressive_prod.py:143-183.
+ * x, y, out: (batch, 2^n); out must not alias x or y. 1 <= n <= 12.
+ */
+CB_API int cb_bilinear(int op, int mode, const float *x, const float *y, float *out,
+                       int64_t batch, int n, uint32_t neg_mask, uint32_t zero_mask,
+                       void *stream);
+
+/*
+ * Both backward sums of product `op` for upstream gradient g:
+ * grad_a = cb_bilinear(op, GRAD_A, b, g), grad_b = cb_bilinear(op, GRAD_B, a, g).
+ * Replaces the pair of geom_prod_fwd calls in the autograd backward of
+ * extensions/ga/geom_prod.py:241-250 (and its wedge/inner/contract/regressive
+ * counterparts). Either output may be NULL to skip it.
+ */
+CB_API int cb_bilinear_bwd(int op, const float *a, const float *b, const float *g,
+                           float *grad_a, float *grad_b, int64_t batch, int n,
+                           uint32_t neg_mask, uint32_t zero_mask, void *stream);
+
+/* Message of the last failure on this thread ("" if none). */
+CB_API const char *cb_last_error(void);
+
+/*
+ * Synchronises `stream`, then returns CB_ERR_DEVICE (and clears the flag) if a
+ * kernel of this library recorded a device-side failure since the last call,
+ * else CB_OK. The reference had no counterpart (it raised from
+ * C10_CUDA_KERNEL_LAUNCH_CHECK only, e.g. kernels/ga/geom_prod.cu:189).
+ */
+CB_API int cb_device_status(void *stream);
+
+/* Library ABI version (major * 100 + minor). */
+CB_API int cb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CLIFFORDCUDA_B200_H */

@@ -1,0 +1,72 @@
+"""The CPU oracle against the golden fixtures generated from the reference
+(tests/golden/make_golden.py). No GPU."""
+import hashlib
+
+import numpy as np
+import pytest
+
+from oracle import ga_oracle as O
+from tests.helpers import inputs, load_npz, product_cases, rel_l2
+
+CASES = product_cases()
+
+
+@pytest.mark.parametrize("op,metric", CASES, ids=[f"{o}-{m}" for o, m in CASES])
+def test_products_vs_reference(op, metric):
+    P = load_npz("products.npz")
+    key = f"{op}|{','.join(map(str, metric))}"
+    n = len(metric)
+    c, ga, gb = O.forward_backward(op, n, metric, P[key + "|a"], P[key + "|b"], P[key + "|g"])
+    for mine, name in ((c, "c"), (ga, "ga"), (gb, "gb")):
+        ref = P[key + "|" + name]
+        assert np.abs(mine - ref).max() <= 1e-12 * max(1.0, np.abs(ref).max()), name
+
+
+def test_config1_vs_reference():
+    G = load_npz("config1.npz")
+    a, b, _ = inputs(5, int(G["seed"]), 4096)
+    g = np.ones_like(a)
+    c, ga, gb = O.forward_backward("gp", 5, (1,) * 5, a, b, g)
+    for arr, name, i in ((c, "c", 0), (ga, "ga", 1), (gb, "gb", 2)):
+        np.testing.assert_allclose(arr[:64], G[name + "_head"], rtol=0, atol=1e-12)
+        assert abs(arr.sum() - G["sums"][i]) <= 1e-9 * max(1, abs(G["sums"][i]))
+        assert abs(np.linalg.norm(arr) - G["norms"][i]) <= 1e-9 * G["norms"][i]
+
+
+def test_sign_tables_vs_reference():
+    S = load_npz("sigma.npz")
+    for key in S.files:
+        kind, m = key.split("|")
+        if kind != "gp":
+            continue
+        metric = tuple(int(x) for x in m.split(","))
+        t = O.sign_table(len(metric), metric)
+        assert hashlib.sha256(t.tobytes()).digest() == S[key].tobytes(), key
+
+
+@pytest.mark.parametrize("n", [7, 8])
+def test_rotor_vs_reference(n):
+    R = load_npz("rotor.npz")
+    beta, x, y = R[f"{n}|beta"], R[f"{n}|x"], R[f"{n}|y"]
+    assert rel_l2(O.rotor_apply(n, beta, x), y) < 1e-12
+    # the blade-minor form equals the reference's Givens chain
+    chain = O.givens_chain_apply(n, O.rotor_matrix(n, beta), x)
+    assert rel_l2(chain, y) < 1e-12
+
+
+def test_rotor_matrix_orthogonal():
+    rng = np.random.default_rng(3)
+    Rm = O.rotor_matrix(8, rng.standard_normal(28))
+    np.testing.assert_allclose(Rm @ Rm.T, np.eye(8), atol=1e-12)
+    assert abs(np.linalg.det(Rm) - 1) < 1e-12
+
+
+def test_einsum_port_matches_c_oracle():
+    import torch
+    a, b = [np.random.default_rng(5 + i).standard_normal((4, 64)) for i in range(2)]
+    for op in ("gp", "wedge", "inner", "lc", "rc", "reg"):
+        metric = (1, 1, 1, -1, 1, -1)
+        f = O.EinsumProduct(op, 6, metric, dtype=torch.float64)
+        got = f(torch.tensor(a), torch.tensor(b)).numpy()
+        ref = O.regressive_fwd(6, metric, a, b) if op == "reg" else O.product(op, "fwd", 6, metric, a, b)
+        assert rel_l2(got, ref) < 1e-13, op
