@@ -137,10 +137,10 @@ def cpu_port_rate(rows, threads, seed=0):
     return rows / one_pass(rows)
 
 
-def workload_config(n_gpus):
-    return {"workload": "Cl(8,0) geom_prod fwd+bwd (batch-by-batch), 524288 products of "
+def workload_config(n_gpus, per_gpu=PER_GPU_BATCH):
+    return {"workload": f"Cl(8,0) geom_prod fwd+bwd (batch-by-batch), {per_gpu} products of "
                         "256 fp32 blades per GPU (config 3 global batch / 8), N(0,1)",
-            "per_gpu_batch": PER_GPU_BATCH, "global_batch": PER_GPU_BATCH * n_gpus,
+            "per_gpu_batch": per_gpu, "global_batch": per_gpu * n_gpus,
             "dim": D, "metric": [1] * N_GEN,
             "parallelism": f"dp{n_gpus} (row shards, no collective)",
             "l2": "inputs 1.5 GB per GPU > 126 MB L2; no flush needed"}
@@ -176,10 +176,13 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=PER_GPU_BATCH,
+                    help="rows per GPU (profiling runs use a smaller case)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -200,7 +203,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
     metric = (1,) * N_GEN
-    B = PER_GPU_BATCH
+    B = args.batch
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     a = torch.randn(B, D, device=dev, generator=gen)
     b = torch.randn(B, D, device=dev, generator=gen)
@@ -253,7 +256,51 @@ def main():
     achieved = FLOPS_PER_SUM * B / (kernel_ms / 1000.0) / 1e12
     peak = fp32_peak_tflops(dev)
 
-    # ---- end to end through the public API, host (pinned) buffers
+    e2e_value = None
+    if not args.no_e2e:
+        e2e_value = run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier)
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            rows = 8192
+            cpu = {"value": cpu_port_rate(rows, threads), "unit": UNIT, "cores": threads,
+                   "kind": "port",
+                   "sample": f"{rows} Cl(8,0) products fwd+bwd, fp32 torch einsum port of "
+                             f"_shared/_einsum_refs.py, {threads} threads"}
+        traffic = (MEASURED_TRAFFIC_PER_SUM * B) if MEASURED_TRAFFIC_PER_SUM else None
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1), seeded per rank",
+            "config": workload_config(world, B),
+            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": "nominal FP32 CUDA-core peak: SMs x 128 FMA/clk x 2 "
+                                        "x sm_max_mhz of MEASURED_PEAKS.json",
+                         "kernel": "bilinear_tiled_kernel", "kernel_ms_per_launch": kernel_ms,
+                         "hbm_gbs": BYTES_PER_SUM * B / (kernel_ms / 1000.0) / 1e9},
+            "pct_fp32_peak": 100.0 * achieved / peak,
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_value is None else {
+                "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 3 * B * D * 4,
+                "d2h_bytes_per_step": 3 * B * D * 4,
+                "path": "cliffordcuda_b200.geom_prod + autograd backward, pinned host "
+                        "buffers, copies inside the timed region"},
+            "gpu_launches": 3 * K,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier):
+    """Same metric through the public API with pinned host buffers: each step
+    copies a, b, g in, runs geom_prod + backward, copies c, grad_a, grad_b out."""
+    B = a.shape[0]
     ha = a.cpu().pin_memory()
     hb = b.cpu().pin_memory()
     hg = g.cpu().pin_memory()
@@ -285,43 +332,7 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = t.item()
-    e2e_value = world * B * K2 / (e2e_ms / 1000.0)
-
-    if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline:
-            threads = os.cpu_count() or 1
-            rows = 8192
-            cpu = {"value": cpu_port_rate(rows, threads), "unit": UNIT, "cores": threads,
-                   "kind": "port",
-                   "sample": f"{rows} Cl(8,0) products fwd+bwd, fp32 torch einsum port of "
-                             f"_shared/_einsum_refs.py, {threads} threads"}
-        traffic = (MEASURED_TRAFFIC_PER_SUM * B) if MEASURED_TRAFFIC_PER_SUM else None
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic N(0,1), seeded per rank",
-            "config": workload_config(world),
-            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": "nominal FP32 CUDA-core peak: SMs x 128 FMA/clk x 2 "
-                                        "x sm_max_mhz of MEASURED_PEAKS.json",
-                         "kernel": "bilinear_tiled_kernel", "kernel_ms_per_launch": kernel_ms,
-                         "hbm_gbs": BYTES_PER_SUM * B / (kernel_ms / 1000.0) / 1e9},
-            "pct_fp32_peak": 100.0 * achieved / peak,
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 3 * B * D * 4,
-                    "d2h_bytes_per_step": 3 * B * D * 4,
-                    "path": "cliffordcuda_b200.geom_prod + autograd backward, pinned host "
-                            "buffers, copies inside the timed region"},
-            "gpu_launches": 3 * K,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
-
+    return world * B * K2 / (e2e_ms / 1000.0)
 
 if __name__ == "__main__":
     main()

@@ -62,6 +62,11 @@ int device_info(DeviceInfo *out) {
     int dev = 0;
     int st = current_device(&dev);
     if (st) return st;
+    // Bind the device's primary context to the calling thread: callers such
+    // as autograd's backward threads may reach here with no current context,
+    // and the driver-API tensor-map encoder needs one.
+    cudaError_t se = cudaSetDevice(dev);
+    if (se != cudaSuccess) return cuda_fail(se, "cudaSetDevice");
     cudaError_t err = cudaSuccess;
     std::call_once(g_info_once[dev], [&] {
         DeviceInfo d;
