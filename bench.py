@@ -60,7 +60,7 @@ def fp32_peak_tflops(device):
 
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML (read-only) every
-    200 ms while the timed region runs."""
+    50 ms while the timed region runs."""
 
     REASONS = {
         "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
@@ -94,7 +94,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.05)
 
     def __enter__(self):
         if self.h is not None:
@@ -176,7 +176,7 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -17,7 +17,7 @@ namespace {
 constexpr int kThreads = 256;
 
 // One block stages rows of x and y in shared memory and evaluates every term
-// with the sign computed from popcounts. Used for metrics whose low four
+// with the sign computed from popcounts. Used for metrics whose low five
 // generators do not all square to +1, for n < 5 or n > 10, for pointers that
 // are not 16-byte aligned, and for the regressive product, evaluated as
 // dual o wedge o dual (reference _shared/_einsum_refs.py:86-124) with the
@@ -119,7 +119,7 @@ bool use_tiled(int op, int n, uint32_t neg, uint32_t zero, const void *x, const 
                const void *o, int64_t batch) {
     if (op == CB_OP_REG) return false;
     if (n < 5 || n > 10) return false;
-    if ((neg | zero) & 15u) return false;
+    if ((neg | zero) & 31u) return false;  // low five generators Euclidean
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
     if (!al(x) || !al(y) || !al(o)) return false;
     if ((uint64_t)batch * (1u << n) / 32 >= (1ull << 31)) return false;

@@ -11,28 +11,29 @@
 // (reference: extensions/ga/geom_prod.py:216-250 -- the forward LUT and the
 // two transposed backward LUTs -- and the masks of _shared/_einsum_refs.py).
 //
-// Blade indices split into a high part (bits 4..n-1) and a low part (bits
-// 0..3). The sign factorises as
+// Blade indices split into a high part (bits 5..n-1) and a low part (bits
+// 0..4). The sign factorises as
 //     s(P, Q) = s_H(P_h, Q_h) * s_L(P_l, Q_l) * (-1)^(popc(P_h) * popc(Q_l))
 // (every high generator of P passes every low generator of Q; none of the
 // reverse pairs reorder), and every product predicate except the inner
-// product's factorises the same way. The kernel therefore works on 16 x 16
-// register blocks: a thread owns the 16 outputs of one high block k_h of one
-// row and sweeps the high blocks i_h, each step doing up to 256 FFMAs of
+// product's factorises the same way. The kernel therefore works on 32 x 32
+// register blocks: a thread owns the 32 outputs of one high block k_h of one
+// row and sweeps the high blocks i_h, each step doing up to 1024 FFMAs of
 //     acc[k_l] += c(i_l, k_l) * x[i_h, i_l] * y'[i_h ^ k_h, i_l ^ k_l]
 // whose coefficients c in {-1, 0, +1} are compile-time constants (this needs
-// the low four generators to square to +1; other metrics take the generic
-// kernel). The runtime high-part sign and predicate are folded into y' (16
+// the low five generators to square to +1; other metrics take the generic
+// kernel). The runtime high-part sign and predicate are folded into y' (32
 // FMULs per step, read from a per-CTA table); the (-1)^(popc * popc) cross
 // term is either a compile-time body variant chosen by the warp-uniform
 // parity of i_h (forward, grad_b) or a per-lane sign on y' plus a sign on the
 // outputs (grad_a).
 //
-// Data movement: persistent CTAs of 256 threads; a tile is 4096 floats of x
+// Data movement: persistent CTAs of 128 threads; a tile is 4096 floats of x
 // and of y (4096 / 2^n rows), brought in by 2-D TMA loads with 128-byte
 // swizzle into a two-stage mbarrier pipeline; results leave through a
-// swizzled shared tile and a TMA store. The swizzle makes the XOR-indexed
-// 64-byte block reads of y conflict-free in shared memory.
+// swizzled shared tile and a TMA store. A 32-float block is one 128-byte
+// line, and the swizzle makes the XOR-indexed line reads of y (eight lanes
+// of a quarter-warp on eight different lines) conflict-free.
 //
 // The inner product's predicate (P subset Q or Q subset P) does not factor;
 // it is evaluated as left + right contraction minus the doubly counted
@@ -40,27 +41,31 @@
 #pragma once
 #include <algorithm>
 #include <cstdio>
+#include <utility>
 
 #include "common.cuh"
 
 namespace cb {
 namespace tiled {
 
-constexpr int kThreads = 256;
-constexpr int kBlk = 16;                      // low block: 4 generators
+constexpr int kThreads = 128;
+constexpr int kLow = 5;                       // low generators per block
+constexpr int kBlk = 1 << kLow;               // 32 blades per block
 constexpr int kTileFloats = kThreads * kBlk;  // 4096 floats per operand tile
 constexpr int kTileLines = kTileFloats / 32;  // 128 lines of 128 bytes
 constexpr int kTileBytes = kTileFloats * 4;
 
 enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4 };
 
-__host__ __device__ constexpr int popc4(int v) {
-    return (v & 1) + ((v >> 1) & 1) + ((v >> 2) & 1) + ((v >> 3) & 1);
+__host__ __device__ constexpr int popcl(int v) {
+    int c = 0;
+    for (int a = 0; a < kLow; ++a) c += (v >> a) & 1;
+    return c;
 }
 
-__host__ __device__ constexpr int reorder4(int p, int q) {
+__host__ __device__ constexpr int reorderl(int p, int q) {
     int c = 0;
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < kLow; ++a)
         if ((p >> a) & 1)
             for (int b = 0; b < a; ++b) c += (q >> b) & 1;
     return c & 1;
@@ -74,40 +79,67 @@ __host__ __device__ constexpr int low_coef(int il, int kl) {
     const int Q = (MODE == CB_MODE_FWD) ? jl : (MODE == CB_MODE_GRAD_A ? il : kl);
     const bool m = (OPK == OPK_GP)      ? true
                    : (OPK == OPK_WEDGE) ? ((P & Q) == 0)
-                   : (OPK == OPK_LC)    ? ((P & ~Q & 15) == 0)
-                                        : ((Q & ~P & 15) == 0);
+                   : (OPK == OPK_LC)    ? ((P & ~Q & (kBlk - 1)) == 0)
+                                        : ((Q & ~P & (kBlk - 1)) == 0);
     if (!m) return 0;
-    int s = reorder4(P, Q);
+    int s = reorderl(P, Q);
     if (PAR) {
-        if (MODE == CB_MODE_FWD) s ^= popc4(jl) & 1;
-        if (MODE == CB_MODE_GRAD_B) s ^= popc4(kl) & 1;
+        if (MODE == CB_MODE_FWD) s ^= popcl(jl) & 1;
+        if (MODE == CB_MODE_GRAD_B) s ^= popcl(kl) & 1;
     }
     return s ? -1 : 1;
 }
 
+// Coefficient table of one body variant, evaluated by the compiler's
+// constant evaluator; the FMA expansion below emits only the non-zero terms.
+struct CoefTable {
+    signed char c[kBlk * kBlk];
+};
+
+template <int MODE, int OPK, int PAR>
+__host__ __device__ constexpr CoefTable make_coefs() {
+    CoefTable t{};
+    for (int i = 0; i < kBlk * kBlk; ++i) t.c[i] = (signed char)low_coef<MODE, OPK, PAR>(i / kBlk, i % kBlk);
+    return t;
+}
+
+template <int MODE, int OPK, int PAR>
+struct Coefs {
+    static constexpr CoefTable table = make_coefs<MODE, OPK, PAR>();
+};
+
+template <int MODE, int OPK, int PAR, int I>
+__device__ __forceinline__ void fma_term(float (&acc)[kBlk], const float (&xv)[kBlk],
+                                         const float (&yv)[kBlk]) {
+    constexpr int il = I / kBlk, kl = I % kBlk;
+    constexpr int c = Coefs<MODE, OPK, PAR>::table.c[I];
+    if constexpr (c > 0) acc[kl] = fmaf(xv[il], yv[il ^ kl], acc[kl]);
+    else if constexpr (c < 0) acc[kl] = fmaf(-xv[il], yv[il ^ kl], acc[kl]);
+}
+
+template <int MODE, int OPK, int PAR, int... I>
+__device__ __forceinline__ void block_fma_seq(float (&acc)[kBlk], const float (&xv)[kBlk],
+                                              const float (&yv)[kBlk],
+                                              std::integer_sequence<int, I...>) {
+    (fma_term<MODE, OPK, PAR, I>(acc, xv, yv), ...);
+}
+
+// acc[k_l] += c(i_l, k_l) x[i_l] y[i_l ^ k_l] over the block, i_l outer.
 template <int MODE, int OPK, int PAR>
 __device__ __forceinline__ void block_fma(float (&acc)[kBlk], const float (&xv)[kBlk],
                                           const float (&yv)[kBlk]) {
-#pragma unroll
-    for (int il = 0; il < kBlk; ++il)
-#pragma unroll
-        for (int kl = 0; kl < kBlk; ++kl) {
-            const int c = low_coef<MODE, OPK, PAR>(il, kl);
-            if (c > 0) acc[kl] = fmaf(xv[il], yv[il ^ kl], acc[kl]);
-            if (c < 0) acc[kl] = fmaf(-xv[il], yv[il ^ kl], acc[kl]);
-        }
+    block_fma_seq<MODE, OPK, PAR>(acc, xv, yv, std::make_integer_sequence<int, kBlk * kBlk>{});
 }
 
 // Swizzled shared tile: float f of the tile lives in 128-byte line f >> 5, in
 // 16-byte chunk ((f >> 2) & 7) ^ (line & 7) -- the TMA 128B swizzle pattern.
-__device__ __forceinline__ void load_block(const float *tile, int f0, float (&v)[kBlk]) {
-    const int line = f0 >> 5;
-    const int c0 = (f0 >> 2) & 7;
+// A block is one whole line.
+__device__ __forceinline__ void load_block(const float *tile, int line, float (&v)[kBlk]) {
     const float *lp = tile + line * 32;
     const int sw = line & 7;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const float4 q = *reinterpret_cast<const float4 *>(lp + (((c0 + t) ^ sw) << 2));
+    for (int t = 0; t < 8; ++t) {
+        const float4 q = *reinterpret_cast<const float4 *>(lp + ((t ^ sw) << 2));
         v[4 * t + 0] = q.x;
         v[4 * t + 1] = q.y;
         v[4 * t + 2] = q.z;
@@ -115,14 +147,12 @@ __device__ __forceinline__ void load_block(const float *tile, int f0, float (&v)
     }
 }
 
-__device__ __forceinline__ void store_block(float *tile, int f0, const float (&v)[kBlk]) {
-    const int line = f0 >> 5;
-    const int c0 = (f0 >> 2) & 7;
+__device__ __forceinline__ void store_block(float *tile, int line, const float (&v)[kBlk]) {
     float *lp = tile + line * 32;
     const int sw = line & 7;
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
-        *reinterpret_cast<float4 *>(lp + (((c0 + t) ^ sw) << 2)) =
+    for (int t = 0; t < 8; ++t)
+        *reinterpret_cast<float4 *>(lp + ((t ^ sw) << 2)) =
             make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
 }
 
@@ -133,7 +163,7 @@ __device__ __forceinline__ int swz_index(int f) {
 
 __device__ __forceinline__ void apply_sign(float (&yv)[kBlk], float2 sg) {
 #pragma unroll
-    for (int e = 0; e < kBlk; ++e) yv[e] *= (popc4(e) & 1) ? sg.y : sg.x;
+    for (int e = 0; e < kBlk; ++e) yv[e] *= (popcl(e) & 1) ? sg.y : sg.x;
 }
 
 // High-part factor of the step (i_h, k_h) for one predicate: the blade sign
@@ -154,7 +184,7 @@ __device__ __forceinline__ float2 high_factor(int mode, int opk, uint32_t ih, ui
 }
 
 __host__ __device__ inline size_t table_entries(int n, bool inner) {
-    const size_t nh = size_t(1) << (n - 4);
+    const size_t nh = size_t(1) << (n - kLow);
     return nh * nh * (inner ? 2 : 1);
 }
 
@@ -165,21 +195,22 @@ __host__ __device__ inline size_t smem_bytes(int n, bool inner) {
 
 template <int MODE, int OPK>
 __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const float *yt,
-                                      const float2 *tab, const float2 *tab2, int rowf, int kh,
+                                      const float2 *tab, const float2 *tab2, int rowl, int kh,
                                       int lgNH) {
     const int NH = 1 << lgNH;
     // Even-parity i_h first, then odd: the parity-dependent body variant is
     // fixed within each loop (t -> 2t | parity(t) enumerates the even ones,
-    // 2t | !parity(t) the odd ones).
+    // 2t | !parity(t) the odd ones; with a single high block only i_h = 0).
 #pragma unroll 1
     for (int par = 0; par < 2; ++par) {
+        const int count = (NH + 1 - par) >> 1;
 #pragma unroll 1
-        for (int t = 0; t < (NH >> 1); ++t) {
+        for (int t = 0; t < count; ++t) {
             const int ih = (t << 1) | (parity(t) ^ par);
             const int jh = ih ^ kh;
             float xv[kBlk], yv[kBlk];
-            load_block(xt, rowf + ih * kBlk, xv);
-            load_block(yt, rowf + jh * kBlk, yv);
+            load_block(xt, rowl + ih, xv);
+            load_block(yt, rowl + jh, yv);
             const float2 sg = tab[(ih << lgNH) | kh];
             const bool odd = (MODE != CB_MODE_GRAD_A) && par;
             if (OPK == OPK_INNER) {
@@ -208,7 +239,7 @@ __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const
 }
 
 template <int MODE, int OPK>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
     bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
                           const __grid_constant__ CUtensorMap my,
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
@@ -219,7 +250,7 @@ __global__ void __launch_bounds__(kThreads)
     float *xs = reinterpret_cast<float *>(base);  // [2][kTileFloats]
     float *ys = xs + 2 * kTileFloats;             // [2][kTileFloats]
     float *os = ys + 2 * kTileFloats;             // [kTileFloats]
-    const int lgNH = n - 4;
+    const int lgNH = n - kLow;
     const int NH = 1 << lgNH;
     constexpr bool inner = (OPK == OPK_INNER);
     float2 *tab = reinterpret_cast<float2 *>(os + kTileFloats);
@@ -231,8 +262,8 @@ __global__ void __launch_bounds__(kThreads)
     const int D = 1 << n;
     const int r = tid >> lgNH;
     const int kh = tid & (NH - 1);
-    const int rowf = r * D;
-    const uint32_t negH = neg >> 4, zeroH = zero >> 4;
+    const int rowl = (r * D) >> 5;  // first line of this thread's row
+    const uint32_t negH = neg >> kLow, zeroH = zero >> kLow;
 
     if (tid == 0) {
         mbar_init(&full[0], 1);
@@ -275,33 +306,33 @@ __global__ void __launch_bounds__(kThreads)
         float acc[kBlk];
 #pragma unroll
         for (int e = 0; e < kBlk; ++e) acc[e] = 0.0f;
-        sweep<MODE, OPK>(acc, xt, yt, tab, tab2, rowf, kh, lgNH);
+        sweep<MODE, OPK>(acc, xt, yt, tab, tab2, rowl, kh, lgNH);
 
         if (MODE == CB_MODE_GRAD_A && parity(kh)) {
 #pragma unroll
             for (int e = 0; e < kBlk; ++e)
-                if (popc4(e) & 1) acc[e] = -acc[e];
+                if (popcl(e) & 1) acc[e] = -acc[e];
         }
         // inner: remove the P == Q terms counted by both contractions.
         // s(k, k) = s_H(k_h, k_h) s_L(k_l, k_l) (-1)^(popc(k_h) popc(k_l)).
         float dpart = 0.0f;
         if (inner) {
             float xv[kBlk];
-            load_block(xt, rowf + kh * kBlk, xv);
+            load_block(xt, rowl + kh, xv);
             const int shh = blade_sign(kh, kh, negH, zeroH);
             if (MODE == CB_MODE_FWD) {  // out[0] -= sum_i s(i, i) x_i y_i
                 float yv[kBlk];
-                load_block(yt, rowf + kh * kBlk, yv);
+                load_block(yt, rowl + kh, yv);
 #pragma unroll
                 for (int e = 0; e < kBlk; ++e) {
-                    const int sl = (reorder4(e, e) ^ ((popc4(e) & 1) & parity(kh))) ? -1 : 1;
+                    const int sl = (reorderl(e, e) ^ ((popcl(e) & 1) & parity(kh))) ? -1 : 1;
                     dpart = fmaf((float)(shh * sl) * xv[e], yv[e], dpart);
                 }
             } else {  // out[k] -= s(k, k) x_k y_0
-                const float y0 = yt[swz_index(rowf)];
+                const float y0 = yt[swz_index(rowl << 5)];
 #pragma unroll
                 for (int e = 0; e < kBlk; ++e) {
-                    const int sl = (reorder4(e, e) ^ ((popc4(e) & 1) & parity(kh))) ? -1 : 1;
+                    const int sl = (reorderl(e, e) ^ ((popcl(e) & 1) & parity(kh))) ? -1 : 1;
                     acc[e] = fmaf(-(float)(shh * sl) * xv[e], y0, acc[e]);
                 }
             }
@@ -317,7 +348,7 @@ __global__ void __launch_bounds__(kThreads)
                 tma_load_2d(ys + s * kTileFloats, &my, 0, next * kTileLines, &full[s]);
             }
         }
-        store_block(os, rowf + kh * kBlk, acc);
+        store_block(os, rowl + kh, acc);
         if (inner && MODE == CB_MODE_FWD) diag[tid] = dpart;
         fence_proxy_async_smem();
         __syncthreads();
