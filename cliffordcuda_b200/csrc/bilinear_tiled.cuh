@@ -23,15 +23,17 @@
 // whose coefficients c in {-1, 0, +1} are compile-time constants (this needs
 // the low five generators to square to +1; other metrics take the generic
 // kernel). The runtime high-part sign and predicate are folded into y' (32
-// FMULs per step, read from a per-CTA table); the (-1)^(popc * popc) cross
-// term is either a compile-time body variant chosen by the warp-uniform
-// parity of i_h (forward, grad_b) or a per-lane sign on y' plus a sign on the
-// outputs (grad_a).
+// FMULs per step, read from a per-CTA table), and so is the y side of the
+// (-1)^(popc * popc) cross term, which depends only on the parity of y's low
+// index once the step is fixed. What remains of the cross term is a sign on
+// the odd-parity x values (grad_b, 16 FMULs per step) or on the outputs
+// (grad_a). One compile-time body per product and sum keeps the loop small
+// enough for the instruction cache.
 //
 // Data movement: persistent CTAs of 128 threads; a tile is 4096 floats of x
 // and of y (4096 / 2^n rows), brought in by 2-D TMA loads with 128-byte
-// swizzle into a two-stage mbarrier pipeline; results leave through a
-// swizzled shared tile and a TMA store. A 32-float block is one 128-byte
+// swizzle into a two-stage mbarrier pipeline; results are written back into
+// the consumed x tile (swizzled) and leave by a TMA store. A 32-float block is one 128-byte
 // line, and the swizzle makes the XOR-indexed line reads of y (eight lanes
 // of a quarter-warp on eight different lines) conflict-free.
 //
@@ -72,7 +74,7 @@ __host__ __device__ constexpr int reorderl(int p, int q) {
 }
 
 // Coefficient of x[i_l] * y[i_l ^ k_l] in output k_l for the low block.
-template <int MODE, int OPK, int PAR>
+template <int MODE, int OPK>
 __host__ __device__ constexpr int low_coef(int il, int kl) {
     const int jl = il ^ kl;
     const int P = (MODE == CB_MODE_GRAD_A) ? kl : il;
@@ -82,12 +84,7 @@ __host__ __device__ constexpr int low_coef(int il, int kl) {
                    : (OPK == OPK_LC)    ? ((P & ~Q & (kBlk - 1)) == 0)
                                         : ((Q & ~P & (kBlk - 1)) == 0);
     if (!m) return 0;
-    int s = reorderl(P, Q);
-    if (PAR) {
-        if (MODE == CB_MODE_FWD) s ^= popcl(jl) & 1;
-        if (MODE == CB_MODE_GRAD_B) s ^= popcl(kl) & 1;
-    }
-    return s ? -1 : 1;
+    return reorderl(P, Q) ? -1 : 1;
 }
 
 // Coefficient table of one body variant, evaluated by the compiler's
@@ -96,39 +93,39 @@ struct CoefTable {
     signed char c[kBlk * kBlk];
 };
 
-template <int MODE, int OPK, int PAR>
+template <int MODE, int OPK>
 __host__ __device__ constexpr CoefTable make_coefs() {
     CoefTable t{};
-    for (int i = 0; i < kBlk * kBlk; ++i) t.c[i] = (signed char)low_coef<MODE, OPK, PAR>(i / kBlk, i % kBlk);
+    for (int i = 0; i < kBlk * kBlk; ++i) t.c[i] = (signed char)low_coef<MODE, OPK>(i / kBlk, i % kBlk);
     return t;
 }
 
-template <int MODE, int OPK, int PAR>
+template <int MODE, int OPK>
 struct Coefs {
-    static constexpr CoefTable table = make_coefs<MODE, OPK, PAR>();
+    static constexpr CoefTable table = make_coefs<MODE, OPK>();
 };
 
-template <int MODE, int OPK, int PAR, int I>
+template <int MODE, int OPK, int I>
 __device__ __forceinline__ void fma_term(float (&acc)[kBlk], const float (&xv)[kBlk],
                                          const float (&yv)[kBlk]) {
     constexpr int il = I / kBlk, kl = I % kBlk;
-    constexpr int c = Coefs<MODE, OPK, PAR>::table.c[I];
+    constexpr int c = Coefs<MODE, OPK>::table.c[I];
     if constexpr (c > 0) acc[kl] = fmaf(xv[il], yv[il ^ kl], acc[kl]);
     else if constexpr (c < 0) acc[kl] = fmaf(-xv[il], yv[il ^ kl], acc[kl]);
 }
 
-template <int MODE, int OPK, int PAR, int... I>
+template <int MODE, int OPK, int... I>
 __device__ __forceinline__ void block_fma_seq(float (&acc)[kBlk], const float (&xv)[kBlk],
                                               const float (&yv)[kBlk],
                                               std::integer_sequence<int, I...>) {
-    (fma_term<MODE, OPK, PAR, I>(acc, xv, yv), ...);
+    (fma_term<MODE, OPK, I>(acc, xv, yv), ...);
 }
 
 // acc[k_l] += c(i_l, k_l) x[i_l] y[i_l ^ k_l] over the block, i_l outer.
-template <int MODE, int OPK, int PAR>
+template <int MODE, int OPK>
 __device__ __forceinline__ void block_fma(float (&acc)[kBlk], const float (&xv)[kBlk],
                                           const float (&yv)[kBlk]) {
-    block_fma_seq<MODE, OPK, PAR>(acc, xv, yv, std::make_integer_sequence<int, kBlk * kBlk>{});
+    block_fma_seq<MODE, OPK>(acc, xv, yv, std::make_integer_sequence<int, kBlk * kBlk>{});
 }
 
 // Swizzled shared tile: float f of the tile lives in 128-byte line f >> 5, in
@@ -167,8 +164,9 @@ __device__ __forceinline__ void apply_sign(float (&yv)[kBlk], float2 sg) {
 }
 
 // High-part factor of the step (i_h, k_h) for one predicate: the blade sign
-// of the high parts times the high-part predicate; .y adds grad_a's per-lane
-// (-1)^popc(k_h) for odd-parity y elements.
+// of the high parts times the high-part predicate (.x, for even-parity y
+// elements); .y adds the y side of the cross term for odd-parity y elements:
+// (-1)^popc(i_h) for the forward sum and grad_b, (-1)^popc(k_h) for grad_a.
 __device__ __forceinline__ float2 high_factor(int mode, int opk, uint32_t ih, uint32_t kh,
                                               uint32_t negH, uint32_t zeroH) {
     const uint32_t jh = ih ^ kh;
@@ -179,7 +177,7 @@ __device__ __forceinline__ float2 high_factor(int mode, int opk, uint32_t ih, ui
     if (opk == OPK_LC) m = (P & ~Q) == 0;
     if (opk == OPK_RC) m = (Q & ~P) == 0;
     const float s = m ? (float)blade_sign(P, Q, negH, zeroH) : 0.0f;
-    const float so = (mode == CB_MODE_GRAD_A && parity(kh)) ? -s : s;
+    const float so = parity(mode == CB_MODE_GRAD_A ? kh : ih) ? -s : s;
     return make_float2(s, so);
 }
 
@@ -189,7 +187,7 @@ __host__ __device__ inline size_t table_entries(int n, bool inner) {
 }
 
 __host__ __device__ inline size_t smem_bytes(int n, bool inner) {
-    return 1024 /* alignment slack */ + 5 * size_t(kTileBytes) +
+    return 1024 /* alignment slack */ + 4 * size_t(kTileBytes) +
            table_entries(n, inner) * sizeof(float2) + kThreads * sizeof(float) + 64;
 }
 
@@ -198,48 +196,37 @@ __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const
                                       const float2 *tab, const float2 *tab2, int rowl, int kh,
                                       int lgNH) {
     const int NH = 1 << lgNH;
-    // Even-parity i_h first, then odd: the parity-dependent body variant is
-    // fixed within each loop (t -> 2t | parity(t) enumerates the even ones,
-    // 2t | !parity(t) the odd ones; with a single high block only i_h = 0).
 #pragma unroll 1
-    for (int par = 0; par < 2; ++par) {
-        const int count = (NH + 1 - par) >> 1;
-#pragma unroll 1
-        for (int t = 0; t < count; ++t) {
-            const int ih = (t << 1) | (parity(t) ^ par);
-            const int jh = ih ^ kh;
-            float xv[kBlk], yv[kBlk];
-            load_block(xt, rowl + ih, xv);
-            load_block(yt, rowl + jh, yv);
-            const float2 sg = tab[(ih << lgNH) | kh];
-            const bool odd = (MODE != CB_MODE_GRAD_A) && par;
-            if (OPK == OPK_INNER) {
-                const float2 sg2 = tab2[(ih << lgNH) | kh];
-                float y2[kBlk];
+    for (int ih = 0; ih < NH; ++ih) {
+        const int jh = ih ^ kh;
+        float xv[kBlk], yv[kBlk];
+        load_block(xt, rowl + ih, xv);
+        load_block(yt, rowl + jh, yv);
+        if (MODE == CB_MODE_GRAD_B) {  // x side of the cross term
+            const float sx = parity(ih) ? -1.0f : 1.0f;
 #pragma unroll
-                for (int e = 0; e < kBlk; ++e) y2[e] = yv[e];
-                apply_sign(yv, sg);
-                apply_sign(y2, sg2);
-                if (odd) {
-                    block_fma<MODE, OPK_LC, 1>(acc, xv, yv);
-                    block_fma<MODE, OPK_RC, 1>(acc, xv, y2);
-                } else {
-                    block_fma<MODE, OPK_LC, 0>(acc, xv, yv);
-                    block_fma<MODE, OPK_RC, 0>(acc, xv, y2);
-                }
-            } else {
-                apply_sign(yv, sg);
-                if (odd)
-                    block_fma<MODE, OPK, 1>(acc, xv, yv);
-                else
-                    block_fma<MODE, OPK, 0>(acc, xv, yv);
-            }
+            for (int e = 0; e < kBlk; ++e)
+                if (popcl(e) & 1) xv[e] *= sx;
+        }
+        const float2 sg = tab[(ih << lgNH) | kh];
+        if (OPK == OPK_INNER) {
+            const float2 sg2 = tab2[(ih << lgNH) | kh];
+            float y2[kBlk];
+#pragma unroll
+            for (int e = 0; e < kBlk; ++e) y2[e] = yv[e];
+            apply_sign(yv, sg);
+            apply_sign(y2, sg2);
+            block_fma<MODE, OPK_LC>(acc, xv, yv);
+            block_fma<MODE, OPK_RC>(acc, xv, y2);
+        } else {
+            apply_sign(yv, sg);
+            block_fma<MODE, OPK>(acc, xv, yv);
         }
     }
 }
 
 template <int MODE, int OPK>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
                           const __grid_constant__ CUtensorMap my,
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
@@ -247,13 +234,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     extern __shared__ unsigned char smem_raw[];
     const uintptr_t base =
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
-    float *xs = reinterpret_cast<float *>(base);  // [2][kTileFloats]
+    float *xs = reinterpret_cast<float *>(base);  // [2][kTileFloats], x in, then out
     float *ys = xs + 2 * kTileFloats;             // [2][kTileFloats]
-    float *os = ys + 2 * kTileFloats;             // [kTileFloats]
     const int lgNH = n - kLow;
     const int NH = 1 << lgNH;
     constexpr bool inner = (OPK == OPK_INNER);
-    float2 *tab = reinterpret_cast<float2 *>(os + kTileFloats);
+    float2 *tab = reinterpret_cast<float2 *>(ys + 2 * kTileFloats);
     float2 *tab2 = tab + NH * NH;
     float *diag = reinterpret_cast<float *>(tab + table_entries(n, inner));
     uint64_t *full = reinterpret_cast<uint64_t *>(diag + kThreads);
@@ -338,16 +324,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
         }
 
-        if (tid == 0) bulk_wait_read_all();  // previous tile's store has left `os`
-        __syncthreads();                     // stage s consumed by every thread
-        if (tid == 0) {
-            const int next = tile + 2 * gridDim.x;
-            if (next < num_tiles) {
-                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
-                tma_load_2d(xs + s * kTileFloats, &mx, 0, next * kTileLines, &full[s]);
-                tma_load_2d(ys + s * kTileFloats, &my, 0, next * kTileLines, &full[s]);
-            }
-        }
+        __syncthreads();  // every thread is done reading stage s
+        float *os = xs + s * kTileFloats;  // results go into the consumed x tile
         store_block(os, rowl + kh, acc);
         if (inner && MODE == CB_MODE_FWD) diag[tid] = dpart;
         fence_proxy_async_smem();
@@ -364,6 +342,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (tid == 0) {
             tma_store_2d(&mo, os, 0, tile * kTileLines);
             bulk_commit();
+            const int next = tile + 2 * gridDim.x;
+            if (next < num_tiles) {
+                bulk_wait_read_all();  // the store has read stage s's x tile
+                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
+                tma_load_2d(xs + s * kTileFloats, &mx, 0, next * kTileLines, &full[s]);
+                tma_load_2d(ys + s * kTileFloats, &my, 0, next * kTileLines, &full[s]);
+            }
         }
     }
     if (tid == 0) bulk_wait_all();
