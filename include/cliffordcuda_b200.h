@@ -79,6 +79,57 @@ CB_API int cb_bilinear_bwd(int op, const float *a, const float *b, const float *
                            float *grad_a, float *grad_b, int64_t batch, int n,
                            uint32_t neg_mask, uint32_t zero_mask, void *stream);
 
+/* ---------------------------------------------------------------- rotors --
+ * A compiled rotor is two caller-owned device buffers:
+ *   cs    (fp32, cs_floats entries): per grade k = 0..n the C(n,k) x C(n,k)
+ *         matrix C_k[I][J] = det(Rm[I, J]), row-major, grades concatenated,
+ *         blades of a grade in increasing bit-pattern order;
+ *   state (fp64, state_doubles entries): B = 2 (M - M^T), Rm = expm(B), and
+ *         C_k in double precision, kept for the backward pass.
+ * apply maps y_k = x_k C_k, i.e. y = R~ x R with the Euclidean product (the
+ * metric is not used, as in the reference). 2 <= n <= 10.
+ */
+
+/* Sizes of the cs and state buffers for n generators. */
+CB_API int cb_rotor_sizes(int n, int64_t *cs_floats, int64_t *state_doubles);
+
+/*
+ * beta (1, n(n-1)/2) lex-pair bivector -> cs, state. One CTA, fp64.
+ * Replaces eigh_exp_fwd (kernels/rotor/eigh_exp.cu:270-322) followed by
+ * givens_factor_fwd_v2 (kernels/rotor/givens_factor.cu:7-59, :233-238).
+ */
+CB_API int cb_rotor_compile(const float *beta, int n, float *cs, double *state, void *stream);
+
+/*
+ * y = x C (transpose = 0) or y = x C^T (transpose = 1), per grade, over
+ * (batch, 2^n) rows. Replaces givens_mb_perm_packed_fwd
+ * (kernels/rotor/givens_apply_mb_perm_packed.cu:8-70, :295-300).
+ */
+CB_API int cb_rotor_apply(const float *cs, const float *x, float *y, int64_t batch, int n,
+                          int transpose, void *stream);
+
+/* Bytes of workspace cb_rotor_apply_bwd needs for this n and batch. */
+CB_API int cb_rotor_workspace_bytes(int n, int64_t batch, int64_t *bytes);
+
+/*
+ * Backward of apply for upstream gradient g: dx = g C^T (skipped if dx is
+ * NULL) and dcs = sum over the batch of x_k^T g_k (cs_floats entries).
+ * `workspace` holds per-CTA partial sums (size from cb_rotor_workspace_bytes).
+ * Replaces givens_mb_perm_packed_bwd (givens_apply_mb_perm_packed.cu:73-179,
+ * which returned only the Givens-angle gradient and no dx).
+ */
+CB_API int cb_rotor_apply_bwd(const float *cs, const float *x, const float *g, float *dx,
+                              float *dcs, int64_t batch, int n, void *workspace,
+                              int64_t workspace_bytes, void *stream);
+
+/*
+ * dcs -> dbeta (n(n-1)/2 floats) through the minors and the matrix exponential.
+ * One CTA, fp64. Replaces givens_factor_bwd_v2 (givens_factor.cu:61-174) and
+ * eigh_exp_bwd (eigh_exp.cu:79-268, 325-361).
+ */
+CB_API int cb_rotor_compile_bwd(const double *state, const float *dcs, int n, float *dbeta,
+                                void *stream);
+
 /* Message of the last failure on this thread ("" if none). */
 CB_API const char *cb_last_error(void);
 

@@ -70,3 +70,22 @@ def test_einsum_port_matches_c_oracle():
         got = f(torch.tensor(a), torch.tensor(b)).numpy()
         ref = O.regressive_fwd(6, metric, a, b) if op == "reg" else O.product(op, "fwd", 6, metric, a, b)
         assert rel_l2(got, ref) < 1e-13, op
+
+
+def test_rotor_gradient_truth_matches_finite_differences():
+    """The fp64 autograd truth used for the rotor gradients agrees with central
+    differences of the oracle's forward map."""
+    rng = np.random.default_rng(11)
+    n = 7
+    beta = 0.2 * rng.standard_normal(21)
+    x, g = rng.standard_normal((2, 3, 128))
+    y, dx, db = O.rotor_grads_torch(n, beta, x, g)
+    eps = 1e-6
+    for i in (0, 7, 20):
+        bp, bm = beta.copy(), beta.copy()
+        bp[i] += eps
+        bm[i] -= eps
+        fd = ((O.rotor_apply(n, bp, x) - O.rotor_apply(n, bm, x)) * g).sum() / (2 * eps)
+        assert abs(fd - db[i]) <= 1e-6 * max(1.0, abs(db[i]))
+    np.testing.assert_allclose(dx, g @ O.rotor_blade_matrix(n, O.rotor_matrix(n, beta)).T,
+                               atol=1e-12)
