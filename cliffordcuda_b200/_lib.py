@@ -34,6 +34,7 @@ SIGNATURES = {
     "cb_rotor_workspace_bytes": (_i32, [_i32, _i64, ctypes.POINTER(_i64)]),
     "cb_rotor_apply_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _i64, _vp]),
     "cb_rotor_compile_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp]),
+    "cb_rotor_apply_bwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
     "cb_last_error": (ctypes.c_char_p, []),
     "cb_device_status": (_i32, [_vp]),
     "cb_version": (_i32, []),

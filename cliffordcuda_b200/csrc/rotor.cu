@@ -36,6 +36,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -703,4 +704,91 @@ extern "C" int cb_rotor_compile_bwd(const double *state, const float *dcs, int n
     rotor_compile_bwd_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(state, dcs, n, dbeta);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_compile_bwd_kernel");
+}
+
+// --------------------------------------------- backward without allocation --
+// cb_rotor_apply_bwd needs a workspace for the per-CTA partial sums of dC,
+// which the caller allocates. Some callers cannot: a host program that binds
+// only this C ABI from another language and has no device allocator of its
+// own, or a framework whose device memory is all owned by its own pool and
+// that forbids side allocations inside a training step. For them,
+// cb_rotor_apply_bwd_noalloc keeps the partials in this fixed array instead:
+// 2^21 floats (8 MiB), which every GPU that loads the library holds until
+// the process exits. It covers n = 7 and 8, the sizes whose backward uses
+// partial sums; the grid is capped so the partials fit.
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 21;
+static __device__ __align__(256) float g_rotor_bwd_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxScratchDevices = 64;
+static float *g_scratch_addr[kMaxScratchDevices];
+static cudaError_t g_scratch_err[kMaxScratchDevices];
+static std::once_flag g_scratch_once[kMaxScratchDevices];
+
+// Device address of the scratch array on the current device. In host code
+// the array's name is only a host-side stand-in, so the address is fetched
+// once per device, with that device current, and cached.
+int noalloc_scratch(float **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxScratchDevices) {
+        set_error("device ordinal %d out of range", dev);
+        return CB_ERR_UNSUPPORTED;
+    }
+    std::call_once(g_scratch_once[dev], [dev] {
+        void *p = nullptr;
+        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_rotor_bwd_scratch);
+        g_scratch_addr[dev] = (g_scratch_err[dev] == cudaSuccess) ? static_cast<float *>(p) : nullptr;
+    });
+    if (!g_scratch_addr[dev])
+        return cuda_fail(g_scratch_err[dev], "cudaGetSymbolAddress(rotor backward scratch)");
+    *out = g_scratch_addr[dev];
+    return CB_OK;
+}
+
+template <int N>
+int noalloc_bwd(const float *cs, const float *x, const float *g, float *dx, float *dcs,
+                int64_t batch, cudaStream_t s) {
+    const Layout L = make_layout(N);
+    float *scratch = nullptr;
+    int st = noalloc_scratch(&scratch);
+    if (st) return st;
+    int parts = bwd_grid<N>(batch);
+    if (parts <= 0) return cuda_fail(cudaGetLastError(), "rotor backward occupancy");
+    parts = (int)std::min<int64_t>(parts, kNoAllocScratchFloats / L.total);
+    // Every CTA writes all of its partial slot, so nothing needs clearing.
+    rotor_bwd_kernel<N><<<parts, 1 << N, bwd_smem<N>(), s>>>(cs, x, g, dx, scratch, batch);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch rotor_bwd_kernel (no-alloc)");
+    rotor_reduce_kernel<<<(L.total + 255) / 256, 256, 0, s>>>(scratch, parts, L.total, dcs);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_reduce_kernel (no-alloc)");
+}
+
+}  // namespace
+
+extern "C" int cb_rotor_apply_bwd_noalloc(const float *cs, const float *x, const float *g,
+                                          float *dx, float *dcs, int64_t batch, int n,
+                                          void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (n != 7 && n != 8) {
+        set_error("rotor_apply_bwd_noalloc: n = %d unsupported; its fixed 8 MiB scratch "
+                  "covers n = 7 and 8 only (use cb_rotor_apply_bwd with a workspace)", n);
+        return CB_ERR_UNSUPPORTED;
+    }
+    if (batch < 0 || !cs || !dcs || (batch > 0 && (!x || !g))) {
+        set_error("rotor_apply_bwd_noalloc: invalid arguments");
+        return CB_ERR_INVALID;
+    }
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    if (batch == 0) {
+        cudaError_t e = cudaMemsetAsync(dcs, 0, (size_t)make_layout(n).total * sizeof(float), s);
+        return e == cudaSuccess ? CB_OK : cuda_fail(e, "cudaMemsetAsync(dcs)");
+    }
+    return n == 7 ? noalloc_bwd<7>(cs, x, g, dx, dcs, batch, s)
+                  : noalloc_bwd<8>(cs, x, g, dx, dcs, batch, s);
 }

@@ -123,6 +123,22 @@ CB_API int cb_rotor_apply_bwd(const float *cs, const float *x, const float *g, f
                               int64_t workspace_bytes, void *stream);
 
 /*
+ * cb_rotor_apply_bwd without a caller workspace; no counterpart in the
+ * reference. For callers that cannot allocate device memory (a host program
+ * binding only this C ABI with no device allocator of its own, or a framework
+ * that owns all device memory in its own pool and forbids side allocations
+ * inside a step). The per-CTA partial sums live in a fixed 8 MiB array inside
+ * the library, held by every GPU that loads it until the process exits; it
+ * covers n = 7 and 8 (other n return CB_ERR_UNSUPPORTED). Allocates nothing.
+ * The first call on a device looks up that array's device address; make that
+ * first call before any stream capture. All calls share the array, so calls
+ * whose work overlaps on the GPU (other streams, other threads) race.
+ */
+CB_API int cb_rotor_apply_bwd_noalloc(const float *cs, const float *x, const float *g,
+                                      float *dx, float *dcs, int64_t batch, int n,
+                                      void *stream);
+
+/*
  * dcs -> dbeta (n(n-1)/2 floats) through the minors and the matrix exponential.
  * One CTA, fp64. Replaces givens_factor_bwd_v2 (givens_factor.cu:61-174) and
  * eigh_exp_bwd (eigh_exp.cu:79-268, 325-361).
