@@ -156,4 +156,14 @@ int device_info(DeviceInfo *out);  // for the current device; cached
 // 128-byte swizzle. Returns CB_OK or an error status.
 int make_tmap_lines(CUtensorMap *map, const void *base, uint64_t lines, uint32_t box_lines);
 
+// 2-D fp32 tensor map over `outer` rows of `inner` floats (row pitch
+// `row_bytes`), box box_inner x box_outer, 128-byte swizzle.
+int make_tmap_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
+
+// internal bilinear dispatcher (bilinear.cu)
+int bilinear(int op, int mode, const float *x, const float *y, float *out, int64_t batch, int n,
+             uint32_t neg, uint32_t zero, cudaStream_t stream);
+
 }  // namespace cb

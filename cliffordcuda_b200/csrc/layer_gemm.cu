@@ -1,0 +1,673 @@
+// layer_gemm.cu -- shared-weight product layers on the 5th-generation tensor
+// cores (tcgen05, TMEM accumulators, TMA operands), fp32 accuracy by 3xTF32.
+//
+// A product layer computes y = op(x, w) with one weight row w for the whole
+// batch (reference layers.py:43-47, which materialised w.expand_as(x) and ran
+// the batch-by-batch kernel). Because op is bilinear, y = x M(w) with
+//     M(w)[i][:] = op(e_i, w)            (D x D, D = 2^n)
+// and the backward pass is
+//     dX = dY M^T,   G = X^T dY,   dw[k] = sum_i grad_b(e_i, G[i][:])[k]
+// where grad_b is the product's own second-operand backward sum. M and the
+// fold are built with the batch-by-batch bilinear kernel on identity rows, so
+// every product (the regressive one included) uses this path unchanged.
+//
+// GEMMs (D = 128 or 256):
+//   * gemm_kmajor_kernel: Y[rows][D] = A[rows][D] B^T with B given as [N][K]
+//     (Y = X M uses B = M^T, dX = dY M^T uses B = M). One CTA per SM,
+//     128-row tiles, K in 32-float chunks (one 128-byte swizzle atom),
+//     two-stage TMA pipeline, two TMEM accumulators so the epilogue of one
+//     tile overlaps the MMAs of the next.
+//   * gemm_mn_kernel: G[D][D] = X^T dY with K = rows, split over CTAs; both
+//     operands are MN-major in shared memory (128-byte swizzle on 32-byte
+//     atoms, the layout the tf32 MMA requires for MN-major operands); each
+//     CTA writes a D x D partial.
+// Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the
+// MMAs (one lane), warps 2-3 split each landed A/B tile into tf32 hi and lo
+// parts in place, warps 4-7 drain TMEM (tcgen05.ld) to global memory.
+//
+// 3xTF32: every operand v is split as hi = v with the low 13 mantissa bits
+// cleared (exactly representable in tf32) and lo = v - hi (exact in fp32);
+// each k-step issues hi*hi + hi*lo + lo*hi into one fp32 accumulator, which
+// leaves an error near 2^-21 |a||b| per product.
+//
+// All waits are bounded (mbar_wait_bounded): on expiry the kernel records a
+// code in the device error word, stops issuing work, and still frees TMEM.
+#include <algorithm>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace cb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int BM = 128;  // MMA M
+constexpr int BK = 32;   // K chunk of the K-major kernel (128 bytes of fp32)
+constexpr int BKR = 16;  // K chunk (rows) of the MN-major kernel
+
+// ------------------------------------------------------------- tcgen05 PTX --
+// Shared-memory matrix descriptor (sm_100 format: start >> 4 at [0,14),
+// LBO >> 4 at [16,30), SBO >> 4 at [32,46), version 1 at [46,48), layout type
+// at [61,64): 2 = 128-byte swizzle, 1 = 128-byte swizzle on 32-byte atoms).
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)layout << 61;
+    return d;
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row groups 1 KB apart.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
+    return smem_desc(saddr, 16, 1024, kLayoutSW128);
+}
+
+// MN-major tf32 operand. The only shared-memory layout the tf32 MMA accepts
+// for MN-major operands is the 128-byte swizzle on 32-byte atoms (TMA mode
+// SWIZZLE_128B_ATOM_32B): 128-byte lines of 32 MN elements, one per K row,
+// K rows in groups of 4 (512 B, SBO); MN groups of 32 elements LBO apart.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t saddr, uint32_t mn_stride) {
+    return smem_desc(saddr, mn_stride, 512, kLayoutSW128Base32B);
+}
+
+// Instruction descriptor for kind::tf32: f32 accumulate, tf32 A and B.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
+           ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols)
+                 : "memory");
+}
+
+// Split fp32 values in place into tf32 hi (kept in `hi`) and lo (to `lo`).
+__device__ __forceinline__ void split_tf32(float4 *hi, float4 *lo, int count, int t, int nt) {
+    for (int e = t; e < count; e += nt) {
+        float4 v = hi[e];
+        float4 h;
+        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        hi[e] = h;
+        lo[e] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    }
+}
+
+// ------------------------------------------------- K-major GEMM (Y = A B^T) --
+template <int D>
+struct KMajorSmem {
+    static constexpr int A_BYTES = BM * BK * 4;                // 16 KB
+    static constexpr int B_BYTES = D * BK * 4;                 // 32 KB at D = 256
+    static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;    // hi + lo of both
+    static constexpr int NSTAGE = 2;
+    static constexpr int BYTES = 1024 + NSTAGE * STAGE + 256;
+    static constexpr int TMEM_COLS = (2 * D <= 256) ? 256 : 512;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kmajor_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mBhi,
+                       const __grid_constant__ CUtensorMap mBlo, float *__restrict__ Y,
+                       int64_t rows, int num_tiles, int *err) {
+    using S = KMajorSmem<D>;
+    constexpr int NK = D / BK;
+    extern __shared__ unsigned char smem_raw[];
+    const uintptr_t base =
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
+    unsigned char *stage0 = reinterpret_cast<unsigned char *>(base);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + S::NSTAGE * S::STAGE);
+    uint64_t *full = bars, *conv = bars + 2, *empty = bars + 4, *accfull = bars + 6,
+             *accempty = bars + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+    auto Ahi = [&](int s) { return stage0 + s * S::STAGE; };
+    auto Alo = [&](int s) { return stage0 + s * S::STAGE + S::A_BYTES; };
+    auto Bhi = [&](int s) { return stage0 + s * S::STAGE + 2 * S::A_BYTES; };
+    auto Blo = [&](int s) { return stage0 + s * S::STAGE + 2 * S::A_BYTES + S::B_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 64);
+            mbar_init(&empty[s], 1);
+            mbar_init(&accfull[s], 1);
+            mbar_init(&accempty[s], 128);
+        }
+        fence_barrier_init();
+        prefetch_tensormap(&mA);
+        prefetch_tensormap(&mBhi);
+        prefetch_tensormap(&mBlo);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int my_tiles = (num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            for (int lt = 0; lt < my_tiles && ok; ++lt) {
+                const int tile = blockIdx.x + lt * gridDim.x;
+                for (int kc = 0; kc < NK && ok; ++kc, ++it) {
+                    const int s = it & 1;
+                    if (!(ok = mbar_wait_bounded(&empty[s], ((it >> 1) + 1) & 1, err, 0x201))) break;
+                    mbar_arrive_expect_tx(&full[s], S::A_BYTES + 2 * S::B_BYTES);
+                    tma_load_2d(Ahi(s), &mA, kc * BK, tile * BM, &full[s]);
+                    tma_load_2d(Bhi(s), &mBhi, kc * BK, 0, &full[s]);
+                    tma_load_2d(Blo(s), &mBlo, kc * BK, 0, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = idesc_tf32(BM, D, false, false);
+        int it = 0;
+        for (int lt = 0; lt < my_tiles && ok; ++lt) {
+            const int b = lt & 1;
+            if (lane == 0) ok = mbar_wait_bounded(&accempty[b], ((lt >> 1) + 1) & 1, err, 0x202);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t dcol = tmem + b * D;
+            for (int kc = 0; kc < NK && ok; ++kc, ++it) {
+                const int s = it & 1;
+                if (lane == 0) ok = mbar_wait_bounded(&conv[s], (it >> 1) & 1, err, 0x203);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t ah = smem_u32(Ahi(s)), al = smem_u32(Alo(s));
+                    const uint32_t bh = smem_u32(Bhi(s)), bl = smem_u32(Blo(s));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint32_t off = kk * 32;  // 8 fp32 along K
+                        const uint64_t dah = kmajor_desc(ah + off);
+                        const uint64_t dal = kmajor_desc(al + off);
+                        const uint64_t dbh = kmajor_desc(bh + off);
+                        const uint64_t dbl = kmajor_desc(bl + off);
+                        mma_tf32(dcol, dah, dbh, idesc, (kc | kk) ? 1u : 0u);
+                        mma_tf32(dcol, dah, dbl, idesc, 1u);
+                        mma_tf32(dcol, dal, dbh, idesc, 1u);
+                    }
+                    mma_commit(&empty[s]);
+                    if (kc == NK - 1) mma_commit(&accfull[b]);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp < 4) {
+        const int t = threadIdx.x - 64;
+        int it = 0;
+        for (int lt = 0; lt < my_tiles && ok; ++lt) {
+            for (int kc = 0; kc < NK && ok; ++kc, ++it) {
+                const int s = it & 1;
+                if (!(ok = mbar_wait_bounded(&full[s], (it >> 1) & 1, err, 0x204))) break;
+                split_tf32(reinterpret_cast<float4 *>(Ahi(s)), reinterpret_cast<float4 *>(Alo(s)),
+                           S::A_BYTES / 16, t, 64);
+                fence_proxy_async_smem();
+                mbar_arrive(&conv[s]);
+            }
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter of this warp
+        for (int lt = 0; lt < my_tiles && ok; ++lt) {
+            const int tile = blockIdx.x + lt * gridDim.x;
+            const int b = lt & 1;
+            if (!(ok = mbar_wait_bounded(&accfull[b], (lt >> 1) & 1, err, 0x205))) break;
+            tc_fence_after();
+            const int64_t row = (int64_t)tile * BM + q * 32 + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * D;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                float v[32];
+                tmem_ld32(taddr + c * 32, v);
+                if (row < rows) {
+                    float4 *dst = reinterpret_cast<float4 *>(Y + row * D + c * 32);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&accempty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, S::TMEM_COLS);
+}
+
+// ------------------------------------------ MN-major GEMM (G = X^T dY, split-K) --
+// Shared tile of one operand chunk: D/32 boxes of 32 floats (MN) x BKR rows
+// (K), box g (MN elements 32g..32g+31) at g * BKR * 128 bytes.
+constexpr int MN_BOX_BYTES = BKR * 128;  // 2 KB
+constexpr int MN_NSTAGE = 3;
+template <int D>
+struct MNSmem {
+    static constexpr int OP_BYTES = D * BKR * 4;    // 16 KB at D = 256
+    static constexpr int STAGE = 4 * OP_BYTES;      // X hi, X lo, dY hi, dY lo
+    static constexpr int BYTES = 1024 + MN_NSTAGE * STAGE + 256;
+    static constexpr int HALVES = D / BM;           // M = D split into 128-row MMAs
+    static constexpr int TMEM_COLS = (HALVES * D < 32) ? 32 : HALVES * D;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_mn_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mG,
+                   float *__restrict__ partial, int64_t rows, int64_t rows_per_cta, int *err) {
+    using S = MNSmem<D>;
+    constexpr int MN_OP_BYTES = S::OP_BYTES;
+    constexpr int MN_STAGE = S::STAGE;
+    extern __shared__ unsigned char smem_raw[];
+    const uintptr_t base =
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
+    unsigned char *stage0 = reinterpret_cast<unsigned char *>(base);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + MN_NSTAGE * MN_STAGE);
+    uint64_t *full = bars, *conv = bars + MN_NSTAGE, *empty = bars + 2 * MN_NSTAGE,
+             *accfull = bars + 3 * MN_NSTAGE;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * MN_NSTAGE + 1);
+    auto op = [&](int s, int which) { return stage0 + s * MN_STAGE + which * MN_OP_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    const int64_t r1 = std::min<int64_t>(rows, r0 + rows_per_cta);
+    const int nchunks = r1 > r0 ? (int)((r1 - r0 + BKR - 1) / BKR) : 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < MN_NSTAGE; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 64);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accfull, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&mX);
+        prefetch_tensormap(&mG);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int s = c % MN_NSTAGE;
+                if (!(ok = mbar_wait_bounded(&empty[s], ((c / MN_NSTAGE) + 1) & 1, err, 0x211)))
+                    break;
+                mbar_arrive_expect_tx(&full[s], 2 * MN_OP_BYTES);
+                const int row = (int)(r0 + (int64_t)c * BKR);
+                for (int g = 0; g < D / 32; ++g) {
+                    tma_load_2d(op(s, 0) + g * MN_BOX_BYTES, &mX, g * 32, row, &full[s]);
+                    tma_load_2d(op(s, 2) + g * MN_BOX_BYTES, &mG, g * 32, row, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = idesc_tf32(BM, D, true, true);
+        for (int c = 0; c < nchunks && ok; ++c) {
+            const int s = c % MN_NSTAGE;
+            if (lane == 0) ok = mbar_wait_bounded(&conv[s], (c / MN_NSTAGE) & 1, err, 0x212);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t xh = smem_u32(op(s, 0)), xl = smem_u32(op(s, 1));
+                const uint32_t gh = smem_u32(op(s, 2)), gl = smem_u32(op(s, 3));
+#pragma unroll
+                for (int kk = 0; kk < BKR / 8; ++kk) {
+                    const uint32_t koff = kk * 1024;  // next 8 rows of K
+                    const uint64_t dgh = mnmajor_desc(gh + koff, MN_BOX_BYTES);
+                    const uint64_t dgl = mnmajor_desc(gl + koff, MN_BOX_BYTES);
+#pragma unroll
+                    for (int h = 0; h < S::HALVES; ++h) {  // i in [128h, 128h + 128)
+                        const uint32_t moff = h * 4 * MN_BOX_BYTES + koff;
+                        const uint64_t dxh = mnmajor_desc(xh + moff, MN_BOX_BYTES);
+                        const uint64_t dxl = mnmajor_desc(xl + moff, MN_BOX_BYTES);
+                        const uint32_t dcol = tmem + h * D;
+                        mma_tf32(dcol, dxh, dgh, idesc, (c | kk) ? 1u : 0u);
+                        mma_tf32(dcol, dxh, dgl, idesc, 1u);
+                        mma_tf32(dcol, dxl, dgh, idesc, 1u);
+                    }
+                }
+                mma_commit(&empty[s]);
+                if (c == nchunks - 1) mma_commit(accfull);
+            }
+            __syncwarp();
+        }
+    } else if (warp < 4) {
+        const int t = threadIdx.x - 64;
+        for (int c = 0; c < nchunks && ok; ++c) {
+            const int s = c % MN_NSTAGE;
+            if (!(ok = mbar_wait_bounded(&full[s], (c / MN_NSTAGE) & 1, err, 0x213))) break;
+            split_tf32(reinterpret_cast<float4 *>(op(s, 0)), reinterpret_cast<float4 *>(op(s, 1)),
+                       MN_OP_BYTES / 16, t, 64);
+            split_tf32(reinterpret_cast<float4 *>(op(s, 2)), reinterpret_cast<float4 *>(op(s, 3)),
+                       MN_OP_BYTES / 16, t, 64);
+            fence_proxy_async_smem();
+            mbar_arrive(&conv[s]);
+        }
+    } else {
+        const int q = warp & 3;
+        float *dst0 = partial + (size_t)blockIdx.x * D * D;
+        if (nchunks > 0 && (ok = mbar_wait_bounded(accfull, 0, err, 0x214))) {
+            tc_fence_after();
+            for (int h = 0; h < S::HALVES; ++h) {
+                const int i = h * 128 + q * 32 + lane;
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + h * D;
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(taddr + c * 32, v);
+                    float4 *dst = reinterpret_cast<float4 *>(dst0 + (size_t)i * D + c * 32);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                }
+            }
+        } else if (nchunks == 0) {
+            for (int h = 0; h < S::HALVES; ++h) {
+                const int i = h * 128 + q * 32 + lane;
+                for (int k = 0; k < D; ++k) dst0[(size_t)i * D + k] = 0.0f;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, S::TMEM_COLS);
+}
+
+// ---------------------------------------------------------- small helpers --
+__global__ void fill_identity_kernel(float *I, int D) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < D * D) I[e] = (e / D == e % D) ? 1.0f : 0.0f;
+}
+
+__global__ void repeat_row_kernel(const float *w, float *W, int D) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < D * D) W[e] = w[e % D];
+}
+
+// mats = [Bf_hi | Bf_lo | Bd_hi | Bd_lo], Bf[k][i] = M[i][k], Bd[i][k] = M[i][k].
+__global__ void split_mats_kernel(const float *M, float *mats, int D) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= D * D) return;
+    const int i = e / D, k = e % D;
+    const float v = M[e];
+    const float hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    const float lo = v - hi;
+    const size_t DD = (size_t)D * D;
+    mats[(size_t)k * D + i] = hi;
+    mats[DD + (size_t)k * D + i] = lo;
+    mats[2 * DD + e] = hi;
+    mats[3 * DD + e] = lo;
+}
+
+// G[e] = sum over partials, accumulated in double in a fixed order.
+__global__ void reduce_partials_kernel(const float *partial, int parts, int DD, float *G) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= DD) return;
+    double s = 0.0;
+    for (int p = 0; p < parts; ++p) s += (double)partial[(size_t)p * DD + e];
+    G[e] = (float)s;
+}
+
+__global__ void column_sum_kernel(const float *A, int D, float *out) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= D) return;
+    float s = 0.0f;
+    for (int i = 0; i < D; ++i) s += A[(size_t)i * D + k];
+    out[k] = s;
+}
+
+bool gemm_supported(int n) { return n == 7 || n == 8; }
+
+int check_layer(int op, int n, uint32_t neg, uint32_t zero) {
+    if (op < CB_OP_GP || op > CB_OP_REG) {
+        set_error("layer: op %d out of range", op);
+        return CB_ERR_INVALID;
+    }
+    if (!gemm_supported(n)) {
+        set_error("layer GEMM path supports n = 7 and 8; got n = %d", n);
+        return CB_ERR_UNSUPPORTED;
+    }
+    const uint32_t nmask = (1u << n) - 1;
+    if ((neg & ~nmask) || (zero & ~nmask) || (neg & zero) || (op == CB_OP_REG && zero)) {
+        set_error("layer: invalid metric masks for op %d", op);
+        return CB_ERR_INVALID;
+    }
+    return CB_OK;
+}
+
+// Split of the batch for G = X^T dY: about 512 rows per partial keeps the
+// fp32 accumulation in TMEM short (the partials are summed in double), at
+// most 8 partials per SM.
+constexpr int kRowsPerPart = 512;
+int mn_parts(const DeviceInfo &di, int64_t batch) {
+    const int64_t want = (batch + kRowsPerPart - 1) / kRowsPerPart;
+    return (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)8 * di.sm_count, want));
+}
+
+// workspace: I | Wrep | M | fold | G | partials (floats)
+size_t layer_ws_floats(int n, int parts) {
+    const size_t DD = (size_t)1 << (2 * n);
+    return 5 * DD + (size_t)parts * DD;
+}
+
+template <int D>
+int launch_kmajor(const float *A, const float *Bhi, const float *Blo, float *Y, int64_t rows,
+                  cudaStream_t s) {
+    if (rows == 0) return CB_OK;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    int *err = nullptr;
+    if ((st = device_error_word(&err))) return st;
+    CUtensorMap mA, mBh, mBl;
+    if ((st = make_tmap_2d(&mA, A, D, rows, D * 4, BK, BM))) return st;
+    if ((st = make_tmap_2d(&mBh, Bhi, D, D, D * 4, BK, D))) return st;
+    if ((st = make_tmap_2d(&mBl, Blo, D, D, D * 4, BK, D))) return st;
+    using S = KMajorSmem<D>;
+    auto kern = gemm_kmajor_kernel<D>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_kmajor)");
+    const int64_t tiles = (rows + BM - 1) / BM;
+    if (tiles > (1 << 30)) {
+        set_error("layer: batch too large");
+        return CB_ERR_UNSUPPORTED;
+    }
+    const int grid = (int)std::min<int64_t>(tiles, di.sm_count);
+    kern<<<grid, kThreads, S::BYTES, s>>>(mA, mBh, mBl, Y, rows, (int)tiles, err);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gemm_kmajor_kernel");
+}
+
+template <int D>
+int launch_mn(const float *x, const float *dy, float *partial, int64_t batch, int parts,
+              cudaStream_t s) {
+    int *err = nullptr;
+    int st = device_error_word(&err);
+    if (st) return st;
+    CUtensorMap mX, mG;
+    if ((st = make_tmap_2d(&mX, x, D, batch, D * 4, 32, BKR, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)))
+        return st;
+    if ((st = make_tmap_2d(&mG, dy, D, batch, D * 4, 32, BKR, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)))
+        return st;
+    auto kern = gemm_mn_kernel<D>;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MNSmem<D>::BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_mn)");
+    const int64_t chunks = (batch + BKR - 1) / BKR;
+    const int64_t rows_per_cta = ((chunks + parts - 1) / parts) * BKR;
+    kern<<<parts, kThreads, MNSmem<D>::BYTES, s>>>(mX, mG, partial, batch, rows_per_cta, err);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gemm_mn_kernel");
+}
+
+}  // namespace
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_layer_workspace_bytes(int n, int64_t batch, int64_t *bytes) {
+    if (!gemm_supported(n)) {
+        set_error("layer GEMM path supports n = 7 and 8; got n = %d", n);
+        return CB_ERR_UNSUPPORTED;
+    }
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    *bytes = (int64_t)layer_ws_floats(n, mn_parts(di, std::max<int64_t>(batch, 1))) * 4;
+    return CB_OK;
+}
+
+extern "C" int cb_layer_prepare(int op, const float *w, int n, uint32_t neg_mask,
+                                uint32_t zero_mask, float *mats, void *workspace,
+                                int64_t workspace_bytes, void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int st = check_layer(op, n, neg_mask, zero_mask);
+    if (st) return st;
+    const int D = 1 << n;
+    const size_t DD = (size_t)D * D;
+    if (!w || !mats || !workspace || workspace_bytes < (int64_t)(3 * DD * 4)) {
+        set_error("layer_prepare: invalid arguments or workspace too small");
+        return CB_ERR_INVALID;
+    }
+    float *I = static_cast<float *>(workspace), *W = I + DD, *M = W + DD;
+    const int blocks = (int)((DD + 255) / 256);
+    fill_identity_kernel<<<blocks, 256, 0, s>>>(I, D);
+    repeat_row_kernel<<<blocks, 256, 0, s>>>(w, W, D);
+    if ((st = bilinear(op, CB_MODE_FWD, I, W, M, D, n, neg_mask, zero_mask, s))) return st;
+    split_mats_kernel<<<blocks, 256, 0, s>>>(M, mats, D);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch layer prepare kernels");
+}
+
+extern "C" int cb_layer_forward(const float *mats, const float *x, float *y, int64_t batch, int n,
+                                void *stream) {
+    if (!gemm_supported(n)) {
+        set_error("layer GEMM path supports n = 7 and 8; got n = %d", n);
+        return CB_ERR_UNSUPPORTED;
+    }
+    if (batch < 0 || (batch > 0 && (!mats || !x || !y || x == y))) {
+        set_error("layer_forward: invalid arguments");
+        return CB_ERR_INVALID;
+    }
+    const size_t DD = (size_t)1 << (2 * n);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return n == 8 ? launch_kmajor<256>(x, mats, mats + DD, y, batch, s)
+                  : launch_kmajor<128>(x, mats, mats + DD, y, batch, s);
+}
+
+extern "C" int cb_layer_backward(int op, const float *mats, const float *x, const float *dy,
+                                 float *dx, float *dw, int64_t batch, int n, uint32_t neg_mask,
+                                 uint32_t zero_mask, void *workspace, int64_t workspace_bytes,
+                                 void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int st = check_layer(op, n, neg_mask, zero_mask);
+    if (st) return st;
+    if (batch < 0 || !mats || (batch > 0 && (!x || !dy))) {
+        set_error("layer_backward: invalid arguments");
+        return CB_ERR_INVALID;
+    }
+    const int D = 1 << n;
+    const size_t DD = (size_t)D * D;
+    if (dx && batch > 0) {
+        st = n == 8 ? launch_kmajor<256>(dy, mats + 2 * DD, mats + 3 * DD, dx, batch, s)
+                    : launch_kmajor<128>(dy, mats + 2 * DD, mats + 3 * DD, dx, batch, s);
+        if (st) return st;
+    }
+    if (!dw) return CB_OK;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    const int parts = mn_parts(di, batch);
+    if (!workspace || workspace_bytes < (int64_t)layer_ws_floats(n, parts) * 4) {
+        set_error("layer_backward: workspace of %lld bytes needed",
+                  (long long)layer_ws_floats(n, parts) * 4);
+        return CB_ERR_INVALID;
+    }
+    float *I = static_cast<float *>(workspace);
+    float *fold = I + 3 * DD, *G = I + 4 * DD, *partial = I + 5 * DD;
+    const int blocks = (int)((DD + 255) / 256);
+    cudaError_t e;
+    if (batch > 0) {
+        st = n == 8 ? launch_mn<256>(x, dy, partial, batch, parts, s)
+                    : launch_mn<128>(x, dy, partial, batch, parts, s);
+        if (st) return st;
+        reduce_partials_kernel<<<blocks, 256, 0, s>>>(partial, parts, (int)DD, G);
+    } else {
+        e = cudaMemsetAsync(G, 0, DD * 4, s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(G)");
+    }
+    fill_identity_kernel<<<blocks, 256, 0, s>>>(I, D);
+    if ((st = bilinear(op, CB_MODE_GRAD_B, I, G, fold, D, n, neg_mask, zero_mask, s))) return st;
+    column_sum_kernel<<<(D + 255) / 256, 256, 0, s>>>(fold, D, dw);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch layer fold kernels");
+}

@@ -1,11 +1,81 @@
 """Shared-weight product layers: y = op(x, w) with one weight row for the
-whole batch (reference layers.py:43-47, which materialised
-``w.expand_as(x)`` and ran the batch-by-batch kernel)."""
+whole batch (reference layers.py:43-47, which materialised w.expand_as(x)
+and ran the batch-by-batch kernel, then let autograd sum the per-row weight
+gradients).
+
+For n = 7 and 8 the layer runs as a dense contraction on the tensor cores:
+M(w) is assembled once per call (cb_layer_prepare), the forward is the
+3xTF32 GEMM y = x M, and the backward gives dx = dy M^T and the weight
+gradient folded from G = x^T dy (cb_layer_backward). Other n run the
+batch-by-batch kernel with the weight broadcast, as the reference did.
+"""
 from __future__ import annotations
 
+import ctypes
+
+import torch
+
+from . import _lib
 from . import products as _p
+
+GEMM_N = (7, 8)
+
+
+def _workspace(n, batch, device):
+    wb = ctypes.c_int64()
+    _lib.check(_lib.load().cb_layer_workspace_bytes(n, batch, ctypes.byref(wb)),
+               "cb_layer_workspace_bytes")
+    return torch.empty(max(wb.value, 4), device=device, dtype=torch.uint8)
+
+
+def prepare(op, weight, n, metric):
+    """mats = [M^T hi | M^T lo | M hi | M lo] for the current weight."""
+    neg, zero = _p.metric_masks(metric)
+    D = 1 << n
+    w = weight.detach().contiguous().view(-1)
+    mats = torch.empty(4 * D * D, device=w.device, dtype=torch.float32)
+    ws = _workspace(n, 1, w.device)
+    with torch.cuda.device(w.device):
+        st = _lib.load().cb_layer_prepare(_lib.OPS[op], _lib.ptr(w), n, neg, zero, _lib.ptr(mats),
+                                          _lib.ptr(ws), ws.numel(), _lib.stream_of(w))
+    _lib.check(st, "cb_layer_prepare")
+    return mats
+
+
+class _LayerFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, op, n, metric):
+        mats = prepare(op, weight, n, metric)
+        y = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            st = _lib.load().cb_layer_forward(_lib.ptr(mats), _lib.ptr(x), _lib.ptr(y),
+                                              x.shape[0], n, _lib.stream_of(x))
+        _lib.check(st, "cb_layer_forward")
+        ctx.save_for_backward(x, mats)
+        ctx.op, ctx.n, ctx.metric, ctx.wshape = op, n, metric, weight.shape
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, mats = ctx.saved_tensors
+        dy = dy.contiguous()
+        need_x, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        dx = torch.empty_like(x) if need_x else None
+        dw = torch.empty(1 << ctx.n, device=x.device, dtype=torch.float32) if need_w else None
+        if need_x or need_w:
+            neg, zero = _p.metric_masks(ctx.metric)
+            ws = _workspace(ctx.n, x.shape[0], x.device)
+            with torch.cuda.device(x.device):
+                st = _lib.load().cb_layer_backward(
+                    _lib.OPS[ctx.op], _lib.ptr(mats), _lib.ptr(x), _lib.ptr(dy), _lib.ptr(dx),
+                    _lib.ptr(dw), x.shape[0], ctx.n, neg, zero, _lib.ptr(ws), ws.numel(),
+                    _lib.stream_of(x))
+            _lib.check(st, "cb_layer_backward")
+        return dx, (dw.view(ctx.wshape) if dw is not None else None), None, None, None
 
 
 def layer_product(op, x, weight, n, metric):
+    if n in GEMM_N:
+        return _LayerFn.apply(x.contiguous(), weight, op, n, tuple(metric))
     w = weight.expand_as(x).contiguous()
     return _p._product(op, x, w, metric)

@@ -79,6 +79,34 @@ CB_API int cb_bilinear_bwd(int op, const float *a, const float *b, const float *
                            float *grad_a, float *grad_b, int64_t batch, int n,
                            uint32_t neg_mask, uint32_t zero_mask, void *stream);
 
+/* ---------------------------------------------------------------- layers --
+ * Shared-weight product layers y = op(x, w), w (1, 2^n) shared by the batch
+ * (reference layers.py:30-76). Because op is bilinear, y = x M(w); the
+ * backward is dx = dy M^T and dw = fold(x^T dy). These run as 3xTF32 tcgen05
+ * GEMMs for n = 7 and 8 (other n return CB_ERR_UNSUPPORTED).
+ * `mats` (caller-owned, 4 * 4^n floats) holds M and M^T split into tf32 hi/lo.
+ * The reference materialised w.expand_as(x) (layers.py:46) and ran the
+ * batch-by-batch kernel, then summed the per-row weight gradients.
+ */
+
+/* Bytes of workspace cb_layer_prepare / cb_layer_backward need. */
+CB_API int cb_layer_workspace_bytes(int n, int64_t batch, int64_t *bytes);
+
+/* w -> mats for product `op` (any CB_OP_*) under the metric masks. */
+CB_API int cb_layer_prepare(int op, const float *w, int n, uint32_t neg_mask, uint32_t zero_mask,
+                            float *mats, void *workspace, int64_t workspace_bytes, void *stream);
+
+/* y = x M(w), x and y (batch, 2^n). */
+CB_API int cb_layer_forward(const float *mats, const float *x, float *y, int64_t batch, int n,
+                            void *stream);
+
+/* dx = dy M^T (skipped if dx is NULL); dw (2^n floats) = weight gradient
+ * summed over the batch (skipped if dw is NULL). */
+CB_API int cb_layer_backward(int op, const float *mats, const float *x, const float *dy, float *dx,
+                             float *dw, int64_t batch, int n, uint32_t neg_mask,
+                             uint32_t zero_mask, void *workspace, int64_t workspace_bytes,
+                             void *stream);
+
 /* ---------------------------------------------------------------- rotors --
  * A compiled rotor is two caller-owned device buffers:
  *   cs    (fp32, cs_floats entries): per grade k = 0..n the C(n,k) x C(n,k)

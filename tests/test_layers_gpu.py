@@ -1,0 +1,114 @@
+"""Product layers (GEMM path for n = 7, 8; batch-by-batch kernel otherwise)
+against the oracle: y = op(x, w), dx, and dw = sum over the batch of the
+second-operand gradient, as the reference's expand_as formulation gives
+(layers.py:43-47)."""
+import numpy as np
+import pytest
+import torch
+
+import cliffordcuda_b200 as cc
+from cliffordcuda_b200 import _lib
+from oracle import ga_oracle as O
+from tests.helpers import REL_L2_TOL, rel_l2
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+LAYERS = {"gp": cc.GeometricProductLayer, "wedge": cc.WedgeProductLayer,
+          "inner": cc.InnerProductLayer, "lc": cc.LeftContractionLayer,
+          "rc": cc.RightContractionLayer, "reg": cc.RegressiveProductLayer}
+
+
+def oracle_layer(op, n, metric, x, w, g):
+    wrep = np.repeat(w.reshape(1, -1), x.shape[0], axis=0)
+    y, dx, dwr = O.forward_backward(op, n, metric, x, wrep, g)
+    return y, dx, dwr.sum(axis=0)
+
+
+def run_layer(op, metric, x, w, g):
+    cl = cc.CliffordAlgebra(list(metric), device=DEV)
+    layer = LAYERS[op](cl)
+    with torch.no_grad():
+        layer.weight.copy_(torch.tensor(w, device=DEV).view(1, -1))
+    xt = torch.tensor(x, device=DEV, requires_grad=True)
+    y = layer(xt)
+    y.backward(torch.tensor(g, device=DEV))
+    return (y.detach().cpu().numpy(), xt.grad.cpu().numpy(),
+            layer.weight.grad.cpu().numpy().ravel())
+
+
+@pytest.mark.parametrize("op", ["gp"])
+def test_gemm_layer_forward_small(op):
+    n, metric = 8, (1,) * 8
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((256, 256)).astype(np.float32)
+    w = (rng.standard_normal(256) / 16).astype(np.float32)
+    cl = cc.CliffordAlgebra(list(metric), device=DEV)
+    layer = LAYERS[op](cl)
+    with torch.no_grad():
+        layer.weight.copy_(torch.tensor(w, device=DEV).view(1, -1))
+        y = layer(torch.tensor(x, device=DEV)).cpu().numpy()
+    ref = oracle_layer(op, n, metric, x, w, np.zeros_like(x))[0]
+    assert rel_l2(y, ref) <= REL_L2_TOL
+
+
+@pytest.mark.parametrize("op", list(LAYERS))
+@pytest.mark.parametrize("n,metric", [(8, (1,) * 8), (8, (1,) * 7 + (-1,)),
+                                      (7, (1,) * 6 + (-1,)), (7, (1,) * 6 + (0,)),
+                                      (5, (1, 1, -1, -1, 1)), (6, (1,) * 6)])
+def test_layer_fwd_bwd(op, n, metric):
+    if op == "reg" and 0 in metric:
+        pytest.skip("regressive undefined for degenerate metrics")
+    rng = np.random.default_rng(n * 13 + list(LAYERS).index(op))
+    batch = 1000 + 37
+    D = 1 << n
+    x = rng.standard_normal((batch, D)).astype(np.float32)
+    g = rng.standard_normal((batch, D)).astype(np.float32)
+    w = (rng.standard_normal(D) / np.sqrt(D)).astype(np.float32)
+    got = run_layer(op, metric, x, w, g)
+    ref = oracle_layer(op, n, metric, x, w, g)
+    for name, a, b in zip(("y", "dx", "dw"), got, ref):
+        assert rel_l2(a, b) <= REL_L2_TOL, f"{op} n={n} {metric} {name}: {rel_l2(a, b):.3e}"
+
+
+@pytest.mark.parametrize("batch", [1, 127, 129, 4096 + 5])
+def test_layer_ragged_batches(batch):
+    n, metric = 8, (1,) * 8
+    rng = np.random.default_rng(batch)
+    x = rng.standard_normal((batch, 256)).astype(np.float32)
+    g = rng.standard_normal((batch, 256)).astype(np.float32)
+    w = (rng.standard_normal(256) / 16).astype(np.float32)
+    got = run_layer("gp", metric, x, w, g)
+    ref = oracle_layer("gp", n, metric, x, w, g)
+    for a, b in zip(got, ref):
+        assert rel_l2(a, b) <= REL_L2_TOL
+
+
+def test_layer_config3_shape_properties():
+    """Config 3 per-GPU shape: x (524,288 x 256), w ~ N(0, 1/256), dY ~ N(0,1).
+    Sampled rows of y and dx against the oracle; dw against the batch-by-batch
+    kernel's grad_b summed over the batch (expand_as formulation)."""
+    from cliffordcuda_b200.products import bilinear_raw
+    batch, n, metric = 524_288, 8, (1,) * 8
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(batch, 256, device=DEV, generator=gen)
+    dy = torch.randn(batch, 256, device=DEV, generator=gen)
+    cl = cc.CliffordAlgebra(list(metric), device=DEV)
+    layer = cc.GeometricProductLayer(cl)
+    with torch.no_grad():
+        layer.weight.copy_(torch.randn(1, 256, device=DEV, generator=gen) / 16)
+    xr = x.clone().requires_grad_(True)
+    y = layer(xr)
+    y.backward(dy)
+    rows = torch.randperm(batch, generator=torch.Generator().manual_seed(2))[:64].to(DEV)
+    w = layer.weight.detach().cpu().numpy().ravel()
+    ref_y, ref_dx, _ = oracle_layer("gp", n, metric, x[rows].cpu().numpy(), w,
+                                    dy[rows].cpu().numpy())
+    assert rel_l2(y[rows].detach().cpu().numpy(), ref_y) <= REL_L2_TOL
+    assert rel_l2(xr.grad[rows].cpu().numpy(), ref_dx) <= REL_L2_TOL
+    wrep = layer.weight.detach().expand(batch, 256).contiguous()
+    dw_rows = bilinear_raw("gp", "grad_b", x, dy, n, metric)
+    dw_ref = dw_rows.double().sum(0).cpu().numpy()
+    assert rel_l2(layer.weight.grad.cpu().numpy().ravel(), dw_ref) <= 1e-5
+    del wrep
+    _lib.device_status(DEV)
