@@ -181,8 +181,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--batch", type=int, default=PER_GPU_BATCH,
+    ap.add_argument("--batch", type=int, default=None,
                     help="rows per GPU (profiling runs use a smaller case)")
+    ap.add_argument("--workload", default="headline",
+                    choices=["headline", "products", "layer", "rotor", "pga"],
+                    help="headline = the BASELINE metric; the others measure configs 2-5")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -192,6 +195,12 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    if args.workload != "headline":
+        import bench_configs
+        bench_configs.run(args, world, rank, local)
+        return
+    if args.batch is None:
+        args.batch = PER_GPU_BATCH
 
     import cliffordcuda_b200 as cc
     from cliffordcuda_b200 import _lib

@@ -1,0 +1,278 @@
+"""Measurements of BASELINE configs 2-5 (bench.py --workload ...).
+
+Each workload prints one JSON line with the same timing rules as bench.py's
+headline: W warm-up steps, K timed steps bracketed by a barrier and a device
+synchronisation, CUDA events on the launching stream, max over ranks, clocks
+sampled during the timed region. Inputs are seeded synthetic data of the
+config's shapes, all larger than L2.
+
+  products  config 2: Cl(6,1), all five products fwd + both grads, batch
+            1,048,576 split over the GPUs (strong scaling).
+  layer     config 3: GeometricProductLayer (and Wedge/LeftContraction) in
+            Cl(8,0), x (4,194,304 x 256) split over the GPUs, fwd + dX + dW,
+            dW all-reduced (NCCL) every step.
+  rotor     config 4: RotorLayer train step in Cl(7,1) on 2,097,152 rows split
+            over the GPUs (compile, sandwich, backward to x and the bivector,
+            all-reduce of the bivector gradient); eval (cached compile) apart.
+  pga       config 5: Cl(9,0,1), batch 131,072 split over the GPUs, 10% of rows
+            restricted to grades 0/2/4; geometric product and left contraction.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import statistics
+
+import torch
+
+from bench import ClockSampler, fp32_peak_tflops
+
+PEAKS = {}
+try:
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+        PEAKS = json.load(f)
+except Exception:
+    pass
+HBM_GBS = float(PEAKS.get("hbm_gbs", 6650.0))
+BF16_TFLOPS = float(PEAKS.get("bf16_tflops", 1590.0))
+TF32_TFLOPS = BF16_TFLOPS / 2       # dense tf32 issues at half the bf16 rate
+X3TF32_TFLOPS = TF32_TFLOPS / 3     # three tf32 MMAs per fp32-accurate product
+
+
+def nnz_table(op, n, metric):
+    D = 1 << n
+    zero = sum(1 << t for t, m in enumerate(metric) if m == 0)
+    i = torch.arange(D).view(-1, 1)
+    j = torch.arange(D).view(1, -1)
+    valid = (i & j & zero) == 0
+    if op == "wedge":
+        valid &= (i & j) == 0
+    elif op == "inner":
+        valid &= ((i & ~j) == 0) | ((j & ~i) == 0)
+    elif op == "lc":
+        valid &= (i & ~j) == 0
+    elif op == "rc":
+        valid &= (j & ~i) == 0
+    return int(valid.sum())
+
+
+class Timer:
+    def __init__(self, dev, world):
+        self.dev, self.world = dev, world
+        self.stream = torch.cuda.current_stream(dev)
+
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+
+    def time(self, step, K, W):
+        for _ in range(W):
+            step()
+        torch.cuda.synchronize(self.dev)
+        self.barrier()
+        torch.cuda.synchronize(self.dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(self.dev) as clk:
+            e0.record(self.stream)
+            for _ in range(K):
+                step()
+            e1.record(self.stream)
+            torch.cuda.synchronize(self.dev)
+        self.barrier()
+        ms = e0.elapsed_time(e1)
+        if self.world > 1:
+            t = torch.tensor([ms], device=self.dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = t.item()
+        return ms / K, clk.summary()
+
+
+def _line(args, world, metric, value, unit, ms, clocks, config, extra, scaling="strong"):
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic, seeded", "config": config, "clocks": clocks}
+    line.update(extra)
+    return line
+
+
+def products(args, world, rank, dev, T):
+    from cliffordcuda_b200.products import bilinear_raw
+    n, metric = 7, (1,) * 6 + (-1,)
+    D = 1 << n
+    B = args.batch or (1_048_576 // world)
+    gen = torch.Generator(device=dev).manual_seed(2 + rank)
+    a, b, g = (torch.randn(B, D, device=dev, generator=gen) for _ in range(3))
+    outs = [torch.empty_like(a) for _ in range(3)]
+    per_op = {}
+    total_ms = 0.0
+    for op in ("gp", "wedge", "inner", "lc", "rc"):
+        def step():
+            bilinear_raw(op, "fwd", a, b, n, metric, out=outs[0])
+            bilinear_raw(op, "grad_a", b, g, n, metric, out=outs[1])
+            bilinear_raw(op, "grad_b", a, g, n, metric, out=outs[2])
+        ms, clk = T.time(step, args.steps, args.warmup)
+        total_ms += ms
+        flops = 3 * 2 * nnz_table(op, n, metric) * B
+        bytes_ = 3 * 3 * D * 4 * B
+        per_op[op] = {"products_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
+                      "fp32_tflops": flops / (ms / 1e3) / 1e12,
+                      "pct_fp32_peak": 100 * flops / (ms / 1e3) / 1e12 / fp32_peak_tflops(dev),
+                      "hbm_gbs": bytes_ / (ms / 1e3) / 1e9,
+                      "pct_hbm": 100 * bytes_ / (ms / 1e3) / 1e9 / HBM_GBS}
+    cfg = {"workload": "config 2: Cl(6,1) five products fwd+bwd", "per_gpu_batch": B,
+           "global_batch": B * world, "dim": D, "metric": list(metric),
+           "l2": "inputs 1.5 GB > L2"}
+    return _line(args, world, "Cl(6,1) five products fwd+bwd, products/s (each product)",
+                 world * B / (total_ms / 1e3), "products/s", total_ms, clk, cfg,
+                 {"ops": per_op, "gpu_launches": 15 * args.steps})
+
+
+def layer(args, world, rank, dev, T):
+    import cliffordcuda_b200 as cc
+    n = 8
+    D = 1 << n
+    B = args.batch or (4_194_304 // world)
+    cl = cc.CliffordAlgebra([1] * n, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(3 + rank)
+    x = torch.randn(B, D, device=dev, generator=gen).requires_grad_(True)
+    dy = torch.randn(B, D, device=dev, generator=gen)
+    res = {}
+    main = None
+    for name, cls in (("gp", cc.GeometricProductLayer), ("wedge", cc.WedgeProductLayer),
+                      ("lc", cc.LeftContractionLayer)):
+        lay = cls(cl)
+        with torch.no_grad():
+            lay.weight.copy_(torch.randn(1, D, device=dev, generator=gen) / math.sqrt(D))
+
+        def step():
+            lay.weight.grad = None
+            x.grad = None
+            y = lay(x)
+            y.backward(dy)
+            if world > 1:
+                torch.distributed.all_reduce(lay.weight.grad)
+        ms, clk = T.time(step, args.steps, args.warmup)
+        useful = 3 * 2 * B * D * D
+        res[name] = {"rows_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
+                     "useful_tflops": useful / (ms / 1e3) / 1e12,
+                     "frac_3xtf32_peak": useful / (ms / 1e3) / 1e12 / X3TF32_TFLOPS,
+                     "hbm_gbs": 5 * D * 4 * B / (ms / 1e3) / 1e9}
+        if main is None:
+            main = (ms, clk)
+    ms, clk = main
+    cfg = {"workload": "config 3: GeometricProductLayer fwd+bwd (dX, dW), dW all-reduced",
+           "per_gpu_batch": B, "global_batch": B * world, "dim": D, "metric": [1] * n,
+           "l2": "x, dy 512 MiB each > L2", "parallelism": f"dp{world}"}
+    r = res["gp"]
+    roof = {"bound": "tensor", "achieved": r["useful_tflops"], "peak": X3TF32_TFLOPS,
+            "unit": "TFLOP/s", "frac": r["frac_3xtf32_peak"], "traffic": None,
+            "peak_source": "measured bf16 dense / 2 (tf32) / 3 (3xTF32 MMAs per product)",
+            "tensor_issue_tflops": 3 * r["useful_tflops"], "tf32_peak": TF32_TFLOPS}
+    return _line(args, world, "Cl(8,0) GeometricProductLayer training rows/s",
+                 r["rows_per_s"], "rows/s", ms, clk, cfg,
+                 {"roofline": roof, "layers": res}, scaling="strong")
+
+
+def rotor(args, world, rank, dev, T):
+    import cliffordcuda_b200 as cc
+    n = 8
+    D = 1 << n
+    B = args.batch or (2_097_152 // world)
+    cl = cc.CliffordAlgebra([1] * 7 + [-1], device=dev)
+    gen = torch.Generator(device=dev).manual_seed(4 + rank)
+    lay = cc.RotorLayer(cl)
+    with torch.no_grad():
+        lay.bivector.copy_(0.1 * torch.randn(1, 28, device=dev, generator=gen))
+    x = torch.randn(B, D, device=dev, generator=gen).requires_grad_(True)
+    g = torch.randn(B, D, device=dev, generator=gen)
+    lay.train()
+
+    def step():
+        lay.bivector.grad = None
+        x.grad = None
+        y = lay(x)
+        y.backward(g)
+        if world > 1:
+            torch.distributed.all_reduce(lay.bivector.grad)
+    ms, clk = T.time(step, args.steps, args.warmup)
+    lay.eval()
+    xe = x.detach()
+
+    def eval_step():
+        with torch.no_grad():
+            lay(xe)
+    ms_eval, _ = T.time(eval_step, args.steps, args.warmup)
+
+    def compile_step():
+        with torch.no_grad():
+            cl.compile_bivector(lay.bivector)
+    ms_compile, _ = T.time(compile_step, args.steps, args.warmup)
+    train_bytes = 5 * D * 4 * B
+    eval_bytes = 2 * D * 4 * B
+    cfg = {"workload": "config 4: RotorLayer train step in Cl(7,1)", "per_gpu_batch": B,
+           "global_batch": B * world, "dim": D, "metric": [1] * 7 + [-1],
+           "l2": "x, g 2 GiB each > L2", "parallelism": f"dp{world}"}
+    roof = {"bound": "hbm", "achieved": train_bytes / (ms / 1e3) / 1e9, "peak": HBM_GBS,
+            "unit": "GB/s", "frac": train_bytes / (ms / 1e3) / 1e9 / HBM_GBS, "traffic": None,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+    return _line(args, world, "Cl(7,1) RotorLayer training rows/s", world * B / (ms / 1e3),
+                 "rows/s", ms, clk, cfg,
+                 {"roofline": roof,
+                  "eval": {"rows_per_s": world * B / (ms_eval / 1e3), "ms": ms_eval,
+                           "hbm_gbs": eval_bytes / (ms_eval / 1e3) / 1e9,
+                           "frac_hbm": eval_bytes / (ms_eval / 1e3) / 1e9 / HBM_GBS},
+                  "compile_ms": ms_compile})
+
+
+def pga(args, world, rank, dev, T):
+    from cliffordcuda_b200.products import bilinear_raw
+    n, metric = 10, (1,) * 9 + (0,)
+    D = 1 << n
+    B = args.batch or (131_072 // world)
+    gen = torch.Generator(device=dev).manual_seed(5 + rank)
+    a, b, g = (torch.randn(B, D, device=dev, generator=gen) for _ in range(3))
+    grades = torch.tensor([bin(i).count("1") for i in range(D)], device=dev)
+    even = ((grades == 0) | (grades == 2) | (grades == 4)).float()
+    rows = torch.randperm(B, generator=torch.Generator().manual_seed(9))[: B // 10].to(dev)
+    a[rows] *= even
+    b[rows] *= even
+    outs = [torch.empty_like(a) for _ in range(3)]
+    res = {}
+    total = 0.0
+    for op in ("gp", "lc"):
+        def step():
+            bilinear_raw(op, "fwd", a, b, n, metric, out=outs[0])
+            bilinear_raw(op, "grad_a", b, g, n, metric, out=outs[1])
+            bilinear_raw(op, "grad_b", a, g, n, metric, out=outs[2])
+        ms, clk = T.time(step, args.steps, args.warmup)
+        total += ms
+        flops = 3 * 2 * nnz_table(op, n, metric) * B
+        bytes_ = 9 * D * 4 * B
+        res[op] = {"products_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
+                   "fp32_tflops": flops / (ms / 1e3) / 1e12,
+                   "pct_fp32_peak": 100 * flops / (ms / 1e3) / 1e12 / fp32_peak_tflops(dev),
+                   "hbm_gbs": bytes_ / (ms / 1e3) / 1e9,
+                   "pct_hbm": 100 * bytes_ / (ms / 1e3) / 1e9 / HBM_GBS}
+    cfg = {"workload": "config 5: Cl(9,0,1) gp and lc fwd+bwd, 10% rows even-versor",
+           "per_gpu_batch": B, "global_batch": B * world, "dim": D, "metric": list(metric),
+           "l2": "inputs 1.5 GB > L2"}
+    return _line(args, world, "Cl(9,0,1) gp + lc fwd+bwd products/s", world * B / (total / 1e3),
+                 "products/s", total, clk, cfg, {"ops": res})
+
+
+def run(args, world, rank, local):
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=dev)
+    T = Timer(dev, world)
+    fn = {"products": products, "layer": layer, "rotor": rotor, "pga": pga}[args.workload]
+    line = fn(args, world, rank, dev, T)
+    from cliffordcuda_b200 import _lib
+    _lib.device_status(dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
