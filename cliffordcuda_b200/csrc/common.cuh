@@ -162,6 +162,19 @@ int make_tmap_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t ou
                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
+// internal 3xTF32 tcgen05 GEMMs (layer_gemm.cu), D = 128 or 256:
+//   Y[rows][D] = A[rows][D] * B^T with B = [N][K] given as tf32 hi/lo parts;
+//   partial[p][D][D] = X^T dY over row range p of `parts` ranges;
+//   split_mats: M (D x D) -> [M^T hi | M^T lo | M hi | M lo]; M may alias
+//   the third quarter (M hi) of `mats`.
+int gemm3x_kmajor(int D, const float *A, const float *Bhi, const float *Blo, float *Y,
+                  int64_t rows, cudaStream_t s);
+int gemm3x_mn_parts(int64_t rows);
+int gemm3x_mn(int D, const float *X, const float *dY, float *partial, int64_t rows, int parts,
+              cudaStream_t s);
+int reduce_partials(const float *partial, int parts, int DD, float *G, cudaStream_t s);
+int split_mats(const float *M, float *mats, int D, cudaStream_t s);
+
 // internal bilinear dispatcher (bilinear.cu)
 int bilinear(int op, int mode, const float *x, const float *y, float *out, int64_t batch, int n,
              uint32_t neg, uint32_t zero, cudaStream_t stream);

@@ -455,6 +455,7 @@ __global__ void repeat_row_kernel(const float *w, float *W, int D) {
 }
 
 // mats = [Bf_hi | Bf_lo | Bd_hi | Bd_lo], Bf[k][i] = M[i][k], Bd[i][k] = M[i][k].
+// Each thread reads only M[e] before writing, so M may be the Bd_hi quarter.
 __global__ void split_mats_kernel(const float *M, float *mats, int D) {
     const int e = blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= D * D) return;
@@ -571,6 +572,41 @@ int launch_mn(const float *x, const float *dy, float *partial, int64_t batch, in
 }
 
 }  // namespace
+
+int gemm3x_kmajor(int D, const float *A, const float *Bhi, const float *Blo, float *Y,
+                  int64_t rows, cudaStream_t s) {
+    if (D == 256) return launch_kmajor<256>(A, Bhi, Blo, Y, rows, s);
+    if (D == 128) return launch_kmajor<128>(A, Bhi, Blo, Y, rows, s);
+    set_error("gemm3x_kmajor: D = %d unsupported", D);
+    return CB_ERR_UNSUPPORTED;
+}
+
+int gemm3x_mn_parts(int64_t rows) {
+    DeviceInfo di;
+    if (device_info(&di)) return -1;
+    return mn_parts(di, std::max<int64_t>(rows, 1));
+}
+
+int gemm3x_mn(int D, const float *X, const float *dY, float *partial, int64_t rows, int parts,
+              cudaStream_t s) {
+    if (D == 256) return launch_mn<256>(X, dY, partial, rows, parts, s);
+    if (D == 128) return launch_mn<128>(X, dY, partial, rows, parts, s);
+    set_error("gemm3x_mn: D = %d unsupported", D);
+    return CB_ERR_UNSUPPORTED;
+}
+
+int reduce_partials(const float *partial, int parts, int DD, float *G, cudaStream_t s) {
+    reduce_partials_kernel<<<(DD + 255) / 256, 256, 0, s>>>(partial, parts, DD, G);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch reduce_partials_kernel");
+}
+
+int split_mats(const float *M, float *mats, int D, cudaStream_t s) {
+    split_mats_kernel<<<(D * D + 255) / 256, 256, 0, s>>>(M, mats, D);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch split_mats_kernel");
+}
+
 }  // namespace cb
 
 using namespace cb;

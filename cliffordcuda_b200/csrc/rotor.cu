@@ -17,13 +17,17 @@
 //             C_k[I][J] = det(Rm[I, J]) by Gaussian elimination with partial
 //             pivoting. Per grade k the C(n,k) x C(n,k) matrix is stored
 //             row-major, grades concatenated (C(2n, n) entries in total).
-//   apply:    y_k = x_k C_k per grade (and g_k C_k^T for the x gradient).
-//             A thread owns one column of its grade's matrix, held in
-//             registers; rows are staged in shared memory in grade-sorted,
-//             4-padded order so each float4 load feeds four FFMAs.
-//   backward: one pass over (x, g) gives dx = g C^T and per-CTA partial sums
-//             of dC_k = x_k^T g_k into a caller-provided workspace; a second
-//             kernel sums the partials in a fixed order. The chain to the
+//   apply:    y = x C_full with C_full the D x D matrix holding every C_k at
+//             its blades' (bit-pattern) positions and zeros between grades;
+//             for n = 7, 8 this runs on the tensor cores as the 3xTF32
+//             tcgen05 GEMM of layer_gemm.cu, whose tf32 hi/lo operands
+//             (C_full and its transpose) the compile step appends to cs.
+//             Other n use a generic kernel.
+//   backward: dx = g C_full^T by the same GEMM, and dC_k = x_k^T g_k gathered
+//             from G = x^T g (the split-K tensor-core GEMM, partials summed in
+//             double). The no-allocation variant instead runs a fused
+//             CUDA-core pass (dx and per-CTA partial sums of dC) over a fixed
+//             in-library array. The chain to the
 //             bivector runs in one CTA in fp64:
 //               dRm[p][q] = sum_{I, J} dC[I][J] (-1)^(a+b) det(Rm[I\p, J\q])
 //             (a, b = positions of p in I and q in J; the cofactors are the
@@ -52,7 +56,10 @@ __host__ __device__ inline int binom(int n, int k) {
     return r;
 }
 
-// Per-n layout of the compiled rotor.
+// Per-n layout of the compiled rotor. cs holds the grade blocks (total
+// entries) followed, for the tensor-core sizes, by the GEMM operands
+// [C_full^T hi | C_full^T lo | C_full hi | C_full lo] (4 D^2 entries) from
+// mats_off on.
 struct Layout {
     int n, D;
     int ck[kMaxN + 1];       // C(n, k)
@@ -60,6 +67,9 @@ struct Layout {
     int coff[kMaxN + 2];     // first matrix entry of grade k (sum of C(n,j)^2)
     int padoff[kMaxN + 2];   // first slot of grade k in a 4-padded sorted row
     int total, rowlen;
+    bool tensor;             // n = 7, 8: apply and backward on the tensor cores
+    int mats_off;            // first GEMM operand entry (256-byte aligned for TMA)
+    int64_t cs_floats;       // mats_off + 4 D^2, or total
 };
 
 __host__ __device__ inline Layout make_layout(int n) {
@@ -75,7 +85,32 @@ __host__ __device__ inline Layout make_layout(int n) {
     }
     L.total = L.coff[n + 1];
     L.rowlen = L.padoff[n + 1];
+    L.tensor = (n == 7 || n == 8);
+    L.mats_off = (L.total + 63) & ~63;
+    L.cs_floats = L.tensor ? L.mats_off + 4 * (int64_t)L.D * L.D : L.total;
     return L;
+}
+
+// Rank of blade bp among the blades of its grade in increasing order
+// (colexicographic rank of its set of generators), and the inverse.
+__host__ __device__ inline int blade_rank(uint32_t bp) {
+    int r = 0, i = 0;
+    for (int c = 0; bp; ++c, bp >>= 1)
+        if (bp & 1u) r += binom(c, ++i);
+    return r;
+}
+
+__host__ __device__ inline uint32_t blade_unrank(int n, int k, int r) {
+    uint32_t bp = 0;
+    for (int c = n - 1; c >= 0 && k > 0; --c) {
+        const int b = binom(c, k);
+        if (b <= r) {
+            bp |= 1u << c;
+            r -= b;
+            --k;
+        }
+    }
+    return bp;
 }
 
 __device__ inline int popc(uint32_t v) { return __popc(v); }
@@ -225,78 +260,31 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// ------------------------------------------------------------ apply (fast) --
-// TRANS = 0: out_k = in_k C_k (y from x); TRANS = 1: out_k = in_k C_k^T.
-template <int N, int TRANS>
-__global__ void __launch_bounds__(1 << N)
-    rotor_apply_kernel(const float *__restrict__ cs, const float *__restrict__ in,
-                       float *__restrict__ out, int64_t batch) {
-    constexpr int D = 1 << N;
-    constexpr int MAXC = (N == 7) ? 35 : 70;
-    constexpr int R = 32;  // rows per tile
-    const Layout L = make_layout(N);
-    extern __shared__ float sm[];
-    float *xs = sm;                       // [R][rowlen], grade-sorted, 4-padded
-    float *ys = sm + R * L.rowlen;        // [R][D], bit-pattern order
-    __shared__ int rank[D], blades[D];
-    build_blade_tables(L, rank, blades);
+// C_full[I][J] = C_k[rank I][rank J] for |I| = |J| = k, else 0 (into `M`).
+__global__ void rotor_full_matrix_kernel(const float *__restrict__ cs, int n,
+                                         float *__restrict__ M) {
+    const Layout L = make_layout(n);
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= L.D * L.D) return;
+    const uint32_t I = e / L.D, J = e % L.D;
+    const int k = __popc(I);
+    float v = 0.0f;
+    if (k == __popc(J)) v = cs[L.coff[k] + blade_rank(I) * L.ck[k] + blade_rank(J)];
+    M[e] = v;
+}
 
-    const int t = threadIdx.x;  // grade-sorted index of this thread's column
+// dcs[e] = G[I][J] for every grade-block entry e = (k, rank I, rank J).
+__global__ void rotor_gather_dc_kernel(const float *__restrict__ G, int n,
+                                       float *__restrict__ dcs) {
+    const Layout L = make_layout(n);
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= L.total) return;
     int k = 0;
-    while (t >= L.goff[k + 1]) ++k;
+    while (e >= L.coff[k + 1]) ++k;
     const int ck = L.ck[k];
-    const int col = t - L.goff[k];
-    const int pk = (ck + 3) & ~3;
-    const int xoff = L.padoff[k];
-    const int out_bp = blades[t];
-    constexpr int NREG = (MAXC + 3) / 4 * 4;
-    float creg[NREG];
-#pragma unroll
-    for (int s = 0; s < NREG; ++s) {
-        float v = 0.0f;
-        if (s < ck) v = TRANS ? cs[L.coff[k] + col * ck + s] : cs[L.coff[k] + s * ck + col];
-        creg[s] = v;
-    }
-    // sorted slot of input blade t (bit-pattern index t)
-    const int in_slot = L.padoff[popc(t)] + rank[t];
-    for (int e = t; e < R * L.rowlen; e += D) xs[e] = 0.0f;  // zero the pad slots
-    __syncthreads();
-
-    for (int64_t row0 = (int64_t)blockIdx.x * R; row0 < batch; row0 += (int64_t)gridDim.x * R) {
-#pragma unroll 4
-        for (int r = 0; r < R; ++r) {
-            const int64_t row = row0 + r;
-            xs[r * L.rowlen + in_slot] = (row < batch) ? in[row * D + t] : 0.0f;
-        }
-        __syncthreads();
-#pragma unroll 1
-        for (int r0 = 0; r0 < R; r0 += 4) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int q = 0; q < (MAXC + 3) / 4; ++q) {
-                if (4 * q < pk) {
-#pragma unroll
-                    for (int rr = 0; rr < 4; ++rr) {
-                        const float4 xv =
-                            *reinterpret_cast<const float4 *>(xs + (r0 + rr) * L.rowlen + xoff + 4 * q);
-                        acc[rr] = fmaf(creg[4 * q + 0], xv.x, acc[rr]);
-                        acc[rr] = fmaf(creg[4 * q + 1], xv.y, acc[rr]);
-                        acc[rr] = fmaf(creg[4 * q + 2], xv.z, acc[rr]);
-                        acc[rr] = fmaf(creg[4 * q + 3], xv.w, acc[rr]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int rr = 0; rr < 4; ++rr) ys[(r0 + rr) * D + out_bp] = acc[rr];
-        }
-        __syncthreads();
-#pragma unroll 4
-        for (int r = 0; r < R; ++r) {
-            const int64_t row = row0 + r;
-            if (row < batch) out[row * D + t] = ys[r * D + t];
-        }
-        __syncthreads();
-    }
+    const uint32_t I = blade_unrank(n, k, (e - L.coff[k]) / ck);
+    const uint32_t J = blade_unrank(n, k, (e - L.coff[k]) % ck);
+    dcs[e] = G[(size_t)I * L.D + J];
 }
 
 // --------------------------------------------------- backward (fast, fused) --
@@ -543,21 +531,6 @@ int check_rotor_n(int n) {
     return CB_OK;
 }
 
-template <int N, int TRANS>
-int launch_apply_fast(const float *cs, const float *in, float *out, int64_t batch,
-                      cudaStream_t stream) {
-    const Layout L = make_layout(N);
-    const size_t smem = (size_t)32 * (L.rowlen + L.D) * sizeof(float);
-    auto kern = rotor_apply_kernel<N, TRANS>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rotor_apply)");
-    const int grid = fast_grid(N, batch, 32, (const void *)kern, smem, 1 << N);
-    if (grid < 0) return cuda_fail(cudaGetLastError(), "rotor_apply occupancy");
-    kern<<<grid, 1 << N, smem, stream>>>(cs, in, out, batch);
-    e = cudaGetLastError();
-    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_apply_kernel");
-}
-
 template <int N>
 size_t bwd_smem() {
     const Layout L = make_layout(N);
@@ -582,7 +555,7 @@ extern "C" int cb_rotor_sizes(int n, int64_t *cs_floats, int64_t *state_doubles)
     int st = check_rotor_n(n);
     if (st) return st;
     const Layout L = make_layout(n);
-    if (cs_floats) *cs_floats = L.total;
+    if (cs_floats) *cs_floats = L.cs_floats;
     if (state_doubles) *state_doubles = 2 * n * n + L.total;
     return CB_OK;
 }
@@ -596,9 +569,20 @@ extern "C" int cb_rotor_compile(const float *beta, int n, float *cs, double *sta
     }
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    rotor_compile_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(beta, n, cs, state);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rotor_compile_kernel<<<1, 256, 0, s>>>(beta, n, cs, state);
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_compile_kernel");
+    if (e != cudaSuccess) return cuda_fail(e, "launch rotor_compile_kernel");
+    const Layout L = make_layout(n);
+    if (L.tensor) {  // C_full built in the C_full-hi quarter, then split in place
+        const int DD = L.D * L.D;
+        float *mats = cs + L.mats_off;
+        rotor_full_matrix_kernel<<<(DD + 255) / 256, 256, 0, s>>>(cs, n, mats + 2 * DD);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "launch rotor_full_matrix_kernel");
+        return split_mats(mats + 2 * DD, mats, L.D, s);
+    }
+    return CB_OK;
 }
 
 static int rotor_apply_impl(const float *cs, const float *in, float *out, int64_t batch, int n,
@@ -612,10 +596,13 @@ static int rotor_apply_impl(const float *cs, const float *in, float *out, int64_
     if (batch == 0) return CB_OK;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    if (n == 7) return trans ? launch_apply_fast<7, 1>(cs, in, out, batch, s)
-                             : launch_apply_fast<7, 0>(cs, in, out, batch, s);
-    if (n == 8) return trans ? launch_apply_fast<8, 1>(cs, in, out, batch, s)
-                             : launch_apply_fast<8, 0>(cs, in, out, batch, s);
+    const Layout L = make_layout(n);
+    if (L.tensor) {
+        const int64_t DD = (int64_t)L.D * L.D;
+        const float *mats = cs + L.mats_off;
+        return trans ? gemm3x_kmajor(L.D, in, mats + 2 * DD, mats + 3 * DD, out, batch, s)
+                     : gemm3x_kmajor(L.D, in, mats, mats + DD, out, batch, s);
+    }
     const size_t smem = (size_t)(1 << n) * sizeof(float);
     const int grid = (int)std::min<int64_t>(batch, (int64_t)di.sm_count * 8);
     if (trans)
@@ -637,10 +624,13 @@ extern "C" int cb_rotor_workspace_bytes(int n, int64_t batch, int64_t *bytes) {
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
     const Layout L = make_layout(n);
-    int parts = 0;
-    if (n == 7) parts = bwd_grid<7>(std::max<int64_t>(batch, 1));
-    else if (n == 8) parts = bwd_grid<8>(std::max<int64_t>(batch, 1));
-    *bytes = (int64_t)std::max(parts, 0) * L.total * (int64_t)sizeof(float);
+    int64_t floats = 0;
+    if (L.tensor) {
+        const int parts = gemm3x_mn_parts(batch);
+        if (parts <= 0) return cuda_fail(cudaGetLastError(), "rotor workspace sizing");
+        floats = (int64_t)(parts + 1) * L.D * L.D;  // split-K partials + G
+    }
+    *bytes = floats * (int64_t)sizeof(float);
     return CB_OK;
 }
 
@@ -658,27 +648,30 @@ extern "C" int cb_rotor_apply_bwd(const float *cs, const float *x, const float *
     if ((st = device_info(&di))) return st;
     const Layout L = make_layout(n);
     if (batch == 0) {
-        cudaError_t e = cudaMemsetAsync(dcs, 0, (size_t)L.total * sizeof(float), s);
+        cudaError_t e = cudaMemsetAsync(dcs, 0, (size_t)L.cs_floats * sizeof(float), s);
         return e == cudaSuccess ? CB_OK : cuda_fail(e, "cudaMemsetAsync(dcs)");
     }
-    if (n == 7 || n == 8) {
-        const int parts = (n == 7) ? bwd_grid<7>(batch) : bwd_grid<8>(batch);
-        const int64_t need = (int64_t)parts * L.total * (int64_t)sizeof(float);
+    if (L.tensor) {
+        const int64_t DD = (int64_t)L.D * L.D;
+        const float *mats = cs + L.mats_off;
+        const int parts = gemm3x_mn_parts(batch);
+        const int64_t need = (int64_t)(parts + 1) * DD * (int64_t)sizeof(float);
         if (parts <= 0 || !workspace || workspace_bytes < need) {
             set_error("rotor_apply_bwd: workspace of %lld bytes needed, %lld given",
                       (long long)need, (long long)workspace_bytes);
             return CB_ERR_INVALID;
         }
+        if (dx && (st = gemm3x_kmajor(L.D, g, mats + 2 * DD, mats + 3 * DD, dx, batch, s)))
+            return st;
         float *partial = static_cast<float *>(workspace);
-        if (n == 7)
-            rotor_bwd_kernel<7><<<parts, 128, bwd_smem<7>(), s>>>(cs, x, g, dx, partial, batch);
-        else
-            rotor_bwd_kernel<8><<<parts, 256, bwd_smem<8>(), s>>>(cs, x, g, dx, partial, batch);
+        float *G = partial + (size_t)parts * DD;
+        if ((st = gemm3x_mn(L.D, x, g, partial, batch, parts, s))) return st;
+        if ((st = reduce_partials(partial, parts, (int)DD, G, s))) return st;
+        rotor_gather_dc_kernel<<<(L.total + 255) / 256, 256, 0, s>>>(G, n, dcs);
         cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return cuda_fail(e, "launch rotor_bwd_kernel");
-        rotor_reduce_kernel<<<(L.total + 255) / 256, 256, 0, s>>>(partial, parts, L.total, dcs);
-        e = cudaGetLastError();
-        return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_reduce_kernel");
+        if (e != cudaSuccess) return cuda_fail(e, "launch rotor_gather_dc_kernel");
+        e = cudaMemsetAsync(dcs + L.total, 0, (size_t)(L.cs_floats - L.total) * sizeof(float), s);
+        return e == cudaSuccess ? CB_OK : cuda_fail(e, "cudaMemsetAsync(dcs tail)");
     }
     // generic sizes: dx by the transposed apply, dC by atomics
     if (dx && (st = rotor_apply_impl(cs, g, dx, batch, n, 1, s))) return st;
@@ -764,7 +757,10 @@ int noalloc_bwd(const float *cs, const float *x, const float *g, float *dx, floa
     if (e != cudaSuccess) return cuda_fail(e, "launch rotor_bwd_kernel (no-alloc)");
     rotor_reduce_kernel<<<(L.total + 255) / 256, 256, 0, s>>>(scratch, parts, L.total, dcs);
     e = cudaGetLastError();
-    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_reduce_kernel (no-alloc)");
+    if (e != cudaSuccess) return cuda_fail(e, "launch rotor_reduce_kernel (no-alloc)");
+    // the tensor-core operands appended to cs receive no gradient
+    e = cudaMemsetAsync(dcs + L.total, 0, (size_t)(L.cs_floats - L.total) * sizeof(float), s);
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "cudaMemsetAsync(dcs tail)");
 }
 
 }  // namespace
@@ -786,7 +782,7 @@ extern "C" int cb_rotor_apply_bwd_noalloc(const float *cs, const float *x, const
     int st = device_info(&di);
     if (st) return st;
     if (batch == 0) {
-        cudaError_t e = cudaMemsetAsync(dcs, 0, (size_t)make_layout(n).total * sizeof(float), s);
+        cudaError_t e = cudaMemsetAsync(dcs, 0, (size_t)make_layout(n).cs_floats * sizeof(float), s);
         return e == cudaSuccess ? CB_OK : cuda_fail(e, "cudaMemsetAsync(dcs)");
     }
     return n == 7 ? noalloc_bwd<7>(cs, x, g, dx, dcs, batch, s)
