@@ -38,8 +38,11 @@ NNZ_GP = 4 ** N_GEN                   # non-zeros of the Cl(8,0) sign table
 FLOPS_PER_SUM = 2 * NNZ_GP            # one FMA per non-zero term
 BYTES_PER_SUM = 3 * D * 4             # two operand rows read, one row written
 # DRAM bytes per row of one bilinear_tiled_kernel launch, from ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum / rows). None until captured.
-MEASURED_TRAFFIC_PER_SUM = None
+# (dram__bytes_read.sum + dram__bytes_write.sum of a 65,536-row launch / rows;
+# profiles/bilinear_tiled_cl8_gp.md: (134.3 + 32.1) MB / 65,536). Traffic grows in
+# proportion to rows (every row is read once and written once), so the per-launch
+# figure is this times the batch.
+MEASURED_TRAFFIC_PER_SUM = (134.3e6 + 32.1e6) / 65536
 
 
 def _env_int(k, d):

@@ -14,9 +14,9 @@
 // GEMMs (D = 128 or 256):
 //   * gemm_kmajor_kernel: Y[rows][D] = A[rows][D] B^T with B given as [N][K]
 //     (Y = X M uses B = M^T, dX = dY M^T uses B = M). One CTA per SM,
-//     128-row tiles, K in 32-float chunks (one 128-byte swizzle atom),
-//     two-stage TMA pipeline, two TMEM accumulators so the epilogue of one
-//     tile overlaps the MMAs of the next.
+//     128-row tiles, K in 16-float chunks (64-byte swizzle rows), four-stage
+//     TMA pipeline, two TMEM accumulators so the epilogue of one tile
+//     overlaps the MMAs of the next.
 //   * gemm_mn_kernel: G[D][D] = X^T dY with K = rows, split over CTAs; both
 //     operands are MN-major in shared memory (128-byte swizzle on 32-byte
 //     atoms, the layout the tf32 MMA requires for MN-major operands); each
@@ -42,7 +42,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int BM = 128;  // MMA M
-constexpr int BK = 32;   // K chunk of the K-major kernel (128 bytes of fp32)
+constexpr int BK = 16;   // K chunk of the K-major kernel (64 bytes of fp32)
 constexpr int BKR = 16;  // K chunk (rows) of the MN-major kernel
 
 // ------------------------------------------------------------- tcgen05 PTX --
@@ -50,6 +50,7 @@ constexpr int BKR = 16;  // K chunk (rows) of the MN-major kernel
 // LBO >> 4 at [16,30), SBO >> 4 at [32,46), version 1 at [46,48), layout type
 // at [61,64): 2 = 128-byte swizzle, 1 = 128-byte swizzle on 32-byte atoms).
 constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW64 = 4;
 constexpr uint32_t kLayoutSW128Base32B = 1;
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
                                               uint32_t layout) {
@@ -61,9 +62,10 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     return d;
 }
 
-// K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row groups 1 KB apart.
+// K-major operand, 64-byte swizzle: rows of 64 bytes (16 fp32 of K), 8-row
+// groups 512 B apart.
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
-    return smem_desc(saddr, 16, 1024, kLayoutSW128);
+    return smem_desc(saddr, 16, 512, kLayoutSW64);
 }
 
 // MN-major tf32 operand. The only shared-memory layout the tf32 MMA accepts
@@ -160,7 +162,7 @@ struct KMajorSmem {
     static constexpr int A_BYTES = BM * BK * 4;                // 16 KB
     static constexpr int B_BYTES = D * BK * 4;                 // 32 KB at D = 256
     static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;    // hi + lo of both
-    static constexpr int NSTAGE = 2;
+    static constexpr int NSTAGE = 4;
     static constexpr int BYTES = 1024 + NSTAGE * STAGE + 256;
     static constexpr int TMEM_COLS = (2 * D <= 256) ? 256 : 512;
 };
@@ -177,9 +179,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
     unsigned char *stage0 = reinterpret_cast<unsigned char *>(base);
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + S::NSTAGE * S::STAGE);
-    uint64_t *full = bars, *conv = bars + 2, *empty = bars + 4, *accfull = bars + 6,
-             *accempty = bars + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+    constexpr int NS = S::NSTAGE;
+    uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS,
+             *accempty = bars + 3 * NS + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * NS + 4);
     auto Ahi = [&](int s) { return stage0 + s * S::STAGE; };
     auto Alo = [&](int s) { return stage0 + s * S::STAGE + S::A_BYTES; };
     auto Bhi = [&](int s) { return stage0 + s * S::STAGE + 2 * S::A_BYTES; };
@@ -187,12 +190,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&conv[s], 64);
             mbar_init(&empty[s], 1);
-            mbar_init(&accfull[s], 1);
-            mbar_init(&accempty[s], 128);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accfull[b], 1);
+            mbar_init(&accempty[b], 128);
         }
         fence_barrier_init();
         prefetch_tensormap(&mA);
@@ -213,8 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int lt = 0; lt < my_tiles && ok; ++lt) {
                 const int tile = blockIdx.x + lt * gridDim.x;
                 for (int kc = 0; kc < NK && ok; ++kc, ++it) {
-                    const int s = it & 1;
-                    if (!(ok = mbar_wait_bounded(&empty[s], ((it >> 1) + 1) & 1, err, 0x201))) break;
+                    const int s = it % NS;
+                    if (!(ok = mbar_wait_bounded(&empty[s], ((it / NS) + 1) & 1, err, 0x201))) break;
                     mbar_arrive_expect_tx(&full[s], S::A_BYTES + 2 * S::B_BYTES);
                     tma_load_2d(Ahi(s), &mA, kc * BK, tile * BM, &full[s]);
                     tma_load_2d(Bhi(s), &mBhi, kc * BK, 0, &full[s]);
@@ -233,8 +238,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t dcol = tmem + b * D;
             for (int kc = 0; kc < NK && ok; ++kc, ++it) {
-                const int s = it & 1;
-                if (lane == 0) ok = mbar_wait_bounded(&conv[s], (it >> 1) & 1, err, 0x203);
+                const int s = it % NS;
+                if (lane == 0) ok = mbar_wait_bounded(&conv[s], (it / NS) & 1, err, 0x203);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 tc_fence_after();
@@ -243,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t bh = smem_u32(Bhi(s)), bl = smem_u32(Blo(s));
 #pragma unroll
                     for (int kk = 0; kk < BK / 8; ++kk) {
-                        const uint32_t off = kk * 32;  // 8 fp32 along K
+                        const uint32_t off = kk * 32;  // 8 fp32 along K within a 64-byte row
                         const uint64_t dah = kmajor_desc(ah + off);
                         const uint64_t dal = kmajor_desc(al + off);
                         const uint64_t dbh = kmajor_desc(bh + off);
@@ -263,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int it = 0;
         for (int lt = 0; lt < my_tiles && ok; ++lt) {
             for (int kc = 0; kc < NK && ok; ++kc, ++it) {
-                const int s = it & 1;
-                if (!(ok = mbar_wait_bounded(&full[s], (it >> 1) & 1, err, 0x204))) break;
+                const int s = it % NS;
+                if (!(ok = mbar_wait_bounded(&full[s], (it / NS) & 1, err, 0x204))) break;
                 split_tf32(reinterpret_cast<float4 *>(Ahi(s)), reinterpret_cast<float4 *>(Alo(s)),
                            S::A_BYTES / 16, t, 64);
                 fence_proxy_async_smem();
@@ -531,9 +536,10 @@ int launch_kmajor(const float *A, const float *Bhi, const float *Blo, float *Y, 
     int *err = nullptr;
     if ((st = device_error_word(&err))) return st;
     CUtensorMap mA, mBh, mBl;
-    if ((st = make_tmap_2d(&mA, A, D, rows, D * 4, BK, BM))) return st;
-    if ((st = make_tmap_2d(&mBh, Bhi, D, D, D * 4, BK, D))) return st;
-    if ((st = make_tmap_2d(&mBl, Blo, D, D, D * 4, BK, D))) return st;
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    if ((st = make_tmap_2d(&mA, A, D, rows, D * 4, BK, BM, sw))) return st;
+    if ((st = make_tmap_2d(&mBh, Bhi, D, D, D * 4, BK, D, sw))) return st;
+    if ((st = make_tmap_2d(&mBl, Blo, D, D, D * 4, BK, D, sw))) return st;
     using S = KMajorSmem<D>;
     auto kern = gemm_kmajor_kernel<D>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
