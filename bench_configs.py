@@ -27,6 +27,7 @@ import statistics
 import torch
 
 from bench import ClockSampler, fp32_peak_tflops
+from cliffordcuda_b200.distributed import allreduce_grads
 
 PEAKS = {}
 try:
@@ -151,8 +152,7 @@ def layer(args, world, rank, dev, T):
             x.grad = None
             y = lay(x)
             y.backward(dy)
-            if world > 1:
-                torch.distributed.all_reduce(lay.weight.grad)
+            allreduce_grads(lay)
         ms, clk = T.time(step, args.steps, args.warmup)
         useful = 3 * 2 * B * D * D
         res[name] = {"rows_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
@@ -194,8 +194,7 @@ def rotor(args, world, rank, dev, T):
         x.grad = None
         y = lay(x)
         y.backward(g)
-        if world > 1:
-            torch.distributed.all_reduce(lay.bivector.grad)
+        allreduce_grads(lay)
     ms, clk = T.time(step, args.steps, args.warmup)
     lay.eval()
     xe = x.detach()
