@@ -42,6 +42,7 @@ SIGNATURES = {
     "cb_rotor_apply_bwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
     "cb_last_error": (ctypes.c_char_p, []),
     "cb_device_status": (_i32, [_vp]),
+    "cb_selftest_bounded_wait": (_i32, [_u32, _vp]),
     "cb_version": (_i32, []),
 }
 

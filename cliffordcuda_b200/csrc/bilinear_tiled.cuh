@@ -232,8 +232,9 @@ __global__ void __launch_bounds__(kThreads, 3)
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
                           uint32_t zero, int num_tiles, int *err) {
     extern __shared__ unsigned char smem_raw[];
-    const uintptr_t base =
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
+    // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
+    // the compiler keeps the shared address space (32-bit LDS/STS addressing).
+    unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     float *xs = reinterpret_cast<float *>(base);  // [2][kTileFloats], x in, then out
     float *ys = xs + 2 * kTileFloats;             // [2][kTileFloats]
     const int lgNH = n - kLow;

@@ -175,9 +175,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     using S = KMajorSmem<D>;
     constexpr int NK = D / BK;
     extern __shared__ unsigned char smem_raw[];
-    const uintptr_t base =
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
-    unsigned char *stage0 = reinterpret_cast<unsigned char *>(base);
+    // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
+    // the compiler keeps the shared address space (32-bit LDS/STS addressing).
+    unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    unsigned char *stage0 = base;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + S::NSTAGE * S::STAGE);
     constexpr int NS = S::NSTAGE;
     uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS,
@@ -328,9 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int MN_OP_BYTES = S::OP_BYTES;
     constexpr int MN_STAGE = S::STAGE;
     extern __shared__ unsigned char smem_raw[];
-    const uintptr_t base =
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023);
-    unsigned char *stage0 = reinterpret_cast<unsigned char *>(base);
+    // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
+    // the compiler keeps the shared address space (32-bit LDS/STS addressing).
+    unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    unsigned char *stage0 = base;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + MN_NSTAGE * MN_STAGE);
     uint64_t *full = bars, *conv = bars + MN_NSTAGE, *empty = bars + 2 * MN_NSTAGE,
              *accfull = bars + 3 * MN_NSTAGE;
