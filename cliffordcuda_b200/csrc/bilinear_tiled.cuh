@@ -30,10 +30,15 @@
 // (grad_a). One compile-time body per product and sum keeps the loop small
 // enough for the instruction cache.
 //
-// Data movement: persistent CTAs of 128 threads; a tile is 4096 floats of x
-// and of y (4096 / 2^n rows), brought in by 2-D TMA loads with 128-byte
-// swizzle into a two-stage mbarrier pipeline; results are written back into
-// the consumed x tile (swizzled) and leave by a TMA store. A 32-float block is one 128-byte
+// Data movement: persistent CTAs of four warps; a tile is 4096 floats of x and
+// of y (4096 / 2^n rows), brought in by 2-D TMA loads with 128-byte swizzle
+// into a two-stage mbarrier pipeline. A row's threads share a warp, so each
+// warp reads and writes only its own rows: after its sweep it writes its
+// results into the consumed x tile (swizzled) and counts itself done on the
+// stage; the last warp to finish issues the TMA store of the tile and the
+// next load into the stage. No warp waits on another except through the
+// pipeline (no CTA-wide barrier in the loop, no polling producer warp); the
+// inner product's diagonal correction is a warp-shuffle reduction. A 32-float block is one 128-byte
 // line, and the swizzle makes the XOR-indexed line reads of y (eight lanes
 // of a quarter-warp on eight different lines) conflict-free.
 //
@@ -50,12 +55,13 @@
 namespace cb {
 namespace tiled {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 128;                 // four warps
 constexpr int kLow = 5;                       // low generators per block
 constexpr int kBlk = 1 << kLow;               // 32 blades per block
 constexpr int kTileFloats = kThreads * kBlk;  // 4096 floats per operand tile
 constexpr int kTileLines = kTileFloats / 32;  // 128 lines of 128 bytes
 constexpr int kTileBytes = kTileFloats * 4;
+constexpr int kStages = 2;                    // tiles in flight per CTA
 
 enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4 };
 
@@ -187,8 +193,8 @@ __host__ __device__ inline size_t table_entries(int n, bool inner) {
 }
 
 __host__ __device__ inline size_t smem_bytes(int n, bool inner) {
-    return 1024 /* alignment slack */ + 4 * size_t(kTileBytes) +
-           table_entries(n, inner) * sizeof(float2) + kThreads * sizeof(float) + 64;
+    return 1024 /* alignment slack */ + 2 * kStages * size_t(kTileBytes) +
+           table_entries(n, inner) * sizeof(float2) + 64;
 }
 
 template <int MODE, int OPK>
@@ -235,26 +241,26 @@ __global__ void __launch_bounds__(kThreads, 3)
     // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
     unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    float *xs = reinterpret_cast<float *>(base);  // [2][kTileFloats], x in, then out
-    float *ys = xs + 2 * kTileFloats;             // [2][kTileFloats]
+    float *xs = reinterpret_cast<float *>(base);  // [kStages][kTileFloats], x in, then out
+    float *ys = xs + kStages * kTileFloats;       // [kStages][kTileFloats]
     const int lgNH = n - kLow;
     const int NH = 1 << lgNH;
     constexpr bool inner = (OPK == OPK_INNER);
-    float2 *tab = reinterpret_cast<float2 *>(ys + 2 * kTileFloats);
+    float2 *tab = reinterpret_cast<float2 *>(ys + kStages * kTileFloats);
     float2 *tab2 = tab + NH * NH;
-    float *diag = reinterpret_cast<float *>(tab + table_entries(n, inner));
-    uint64_t *full = reinterpret_cast<uint64_t *>(diag + kThreads);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(tab + table_entries(n, inner));
+    uint64_t *full = bars;
+    int *done_count = reinterpret_cast<int *>(bars + kStages);  // [kStages]
 
     const int tid = threadIdx.x;
     const int D = 1 << n;
-    const int r = tid >> lgNH;
-    const int kh = tid & (NH - 1);
-    const int rowl = (r * D) >> 5;  // first line of this thread's row
     const uint32_t negH = neg >> kLow, zeroH = zero >> kLow;
 
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            done_count[s] = 0;
+        }
         fence_barrier_init();
         prefetch_tensormap(&mx);
         prefetch_tensormap(&my);
@@ -271,8 +277,9 @@ __global__ void __launch_bounds__(kThreads, 3)
         }
     }
     __syncthreads();
+
     if (tid == 0) {
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             const int tile = blockIdx.x + s * gridDim.x;
             if (tile < num_tiles) {
                 mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
@@ -282,12 +289,16 @@ __global__ void __launch_bounds__(kThreads, 3)
         }
     }
 
+    const int r = tid >> lgNH;
+    const int lane = tid & 31;
+    const int kh = tid & (NH - 1);
+    const int rowl = (r * D) >> 5;  // first line of this thread's row
     for (int it = 0;; ++it) {
         const int tile = blockIdx.x + it * gridDim.x;
         if (tile >= num_tiles) break;
-        const int s = it & 1;
-        if (!mbar_wait_bounded(&full[s], (it >> 1) & 1, err, 0x101)) break;
-        const float *xt = xs + s * kTileFloats;
+        const int s = it % kStages;
+        if (!mbar_wait_bounded(&full[s], (it / kStages) & 1, err, 0x101)) break;
+        float *xt = xs + s * kTileFloats;
         const float *yt = ys + s * kTileFloats;
 
         float acc[kBlk];
@@ -302,7 +313,6 @@ __global__ void __launch_bounds__(kThreads, 3)
         }
         // inner: remove the P == Q terms counted by both contractions.
         // s(k, k) = s_H(k_h, k_h) s_L(k_l, k_l) (-1)^(popc(k_h) popc(k_l)).
-        float dpart = 0.0f;
         if (inner) {
             float xv[kBlk];
             load_block(xt, rowl + kh, xv);
@@ -310,11 +320,15 @@ __global__ void __launch_bounds__(kThreads, 3)
             if (MODE == CB_MODE_FWD) {  // out[0] -= sum_i s(i, i) x_i y_i
                 float yv[kBlk];
                 load_block(yt, rowl + kh, yv);
+                float dpart = 0.0f;
 #pragma unroll
                 for (int e = 0; e < kBlk; ++e) {
                     const int sl = (reorderl(e, e) ^ ((popcl(e) & 1) & parity(kh))) ? -1 : 1;
                     dpart = fmaf((float)(shh * sl) * xv[e], yv[e], dpart);
                 }
+                // the row's NH threads are consecutive lanes of one warp
+                for (int m = 1; m < NH; m <<= 1) dpart += __shfl_xor_sync(0xffffffffu, dpart, m);
+                if (kh == 0) acc[0] -= dpart;
             } else {  // out[k] -= s(k, k) x_k y_0
                 const float y0 = yt[swz_index(rowl << 5)];
 #pragma unroll
@@ -324,35 +338,32 @@ __global__ void __launch_bounds__(kThreads, 3)
                 }
             }
         }
-
-        __syncthreads();  // every thread is done reading stage s
-        float *os = xs + s * kTileFloats;  // results go into the consumed x tile
-        store_block(os, rowl + kh, acc);
-        if (inner && MODE == CB_MODE_FWD) diag[tid] = dpart;
+        // This warp's rows are read only by this warp: once its lanes are done
+        // reading, the results can replace the x values of those rows.
+        __syncwarp();
+        store_block(xt, rowl + kh, acc);
         fence_proxy_async_smem();
-        __syncthreads();
-        if (inner && MODE == CB_MODE_FWD) {
-            if (tid < (kThreads >> lgNH)) {
-                float sum = 0.0f;
-                for (int q = 0; q < NH; ++q) sum += diag[(tid << lgNH) + q];
-                os[swz_index(tid * D)] -= sum;
-                fence_proxy_async_smem();
-            }
-            __syncthreads();
-        }
-        if (tid == 0) {
-            tma_store_2d(&mo, os, 0, tile * kTileLines);
-            bulk_commit();
-            const int next = tile + 2 * gridDim.x;
-            if (next < num_tiles) {
-                bulk_wait_read_all();  // the store has read stage s's x tile
-                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
-                tma_load_2d(xs + s * kTileFloats, &mx, 0, next * kTileLines, &full[s]);
-                tma_load_2d(ys + s * kTileFloats, &my, 0, next * kTileLines, &full[s]);
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicAdd(&done_count[s], 1) == kThreads / 32 - 1) {  // last warp
+                __threadfence_block();
+                done_count[s] = 0;
+                tma_store_2d(&mo, xt, 0, tile * kTileLines);
+                bulk_commit();
+                const int next = tile + kStages * gridDim.x;
+                if (next < num_tiles) {
+                    bulk_wait_read_all();  // the store has read stage s's x tile
+                    mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
+                    tma_load_2d(xt, &mx, 0, next * kTileLines, &full[s]);
+                    tma_load_2d(ys + s * kTileFloats, &my, 0, next * kTileLines, &full[s]);
+                }
             }
         }
+        __syncwarp();
     }
-    if (tid == 0) bulk_wait_all();
+    // Stores issued by this thread must finish before the CTA exits.
+    if (lane == 0) bulk_wait_all();
 }
 
 template <int MODE, int OPK>

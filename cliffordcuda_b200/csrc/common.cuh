@@ -87,28 +87,47 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One poll of the phase with parity `phase`. The thread may be suspended
+// inside the instruction until the phase completes or about `hint_ns` pass,
+// so a waiting warp takes no issue slots.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase,
+                                              uint32_t hint_ns = 20000) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(phase)
+        : "r"(smem_u32(bar)), "r"(phase), "r"(hint_ns)
         : "memory");
     return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls, records `code` in the device
-// error word and returns false. try_wait itself suspends for a
-// hardware-defined interval per poll, so the limit bounds wall time to
-// roughly a second or more.
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait: gives up once `timeout_ns` of wall time have passed without
+// the phase completing, records `code` in the device error word and returns
+// false (the caller then stops issuing work; nothing traps).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, int *err,
-                                                  int code, uint32_t limit = (1u << 22)) {
-    for (uint32_t it = 0; it < limit; ++it)
-        if (mbar_try_wait(bar, phase)) return true;
-    atomicCAS(err, 0, code);
-    return false;
+                                                  int code,
+                                                  uint64_t timeout_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, phase)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, phase)) {
+        if (global_timer_ns() - t0 > timeout_ns) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+    return true;
 }
 
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y,

@@ -149,22 +149,22 @@ int make_tmap_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t ou
     return CB_OK;
 }
 
-// One thread waits, with a bound of `limit` polls, on an mbarrier that
+// One thread waits, bounded by `limit_us` microseconds, on an mbarrier that
 // nothing arrives on; the bounded wait records `code` and returns.
-__global__ void bounded_wait_selftest_kernel(uint32_t limit, int *err, int code) {
+__global__ void bounded_wait_selftest_kernel(uint32_t limit_us, int *err, int code) {
     __shared__ uint64_t bar;
     mbar_init(&bar, 1);
     fence_barrier_init();
-    mbar_wait_bounded(&bar, 0, err, code, limit);
+    mbar_wait_bounded(&bar, 0, err, code, (uint64_t)limit_us * 1000ull);
 }
 
 }  // namespace cb
 
-extern "C" int cb_selftest_bounded_wait(uint32_t limit, void *stream) {
+extern "C" int cb_selftest_bounded_wait(uint32_t limit_us, void *stream) {
     int *err = nullptr;
     int st = cb::device_error_word(&err);
     if (st) return st;
-    cb::bounded_wait_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(limit, err,
+    cb::bounded_wait_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(limit_us, err,
                                                                                       0x7f);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cb::cuda_fail(e, "launch bounded_wait_selftest_kernel");

@@ -187,12 +187,12 @@ CB_API int cb_device_status(void *stream);
 
 /*
  * Self-test of the failure path: launches one thread that waits, bounded by
- * `limit` polls, on a barrier nothing completes. The wait gives up, records a
+ * `limit_us` microseconds, on a barrier nothing completes. The wait gives up, records a
  * device-side failure, and the next cb_device_status returns CB_ERR_DEVICE; the
  * context stays usable. No counterpart in the reference (it had no bounded
  * waits).
  */
-CB_API int cb_selftest_bounded_wait(uint32_t limit, void *stream);
+CB_API int cb_selftest_bounded_wait(uint32_t limit_us, void *stream);
 
 /* Library ABI version (major * 100 + minor). */
 CB_API int cb_version(void);
