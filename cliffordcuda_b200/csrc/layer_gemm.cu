@@ -23,7 +23,8 @@
 //     CTA writes a D x D partial.
 // Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the
 // MMAs (one lane), warps 2-3 split each landed A/B tile into tf32 hi and lo
-// parts in place, warps 4-7 drain TMEM (tcgen05.ld) to global memory.
+// parts in place, warps 4-7 drain TMEM (tcgen05.ld) through 128B-swizzled
+// shared staging buffers and TMA-store 32x32 chunks of Y.
 //
 // 3xTF32: every operand v is split as hi = v with the low 13 mantissa bits
 // cleared (exactly representable in tf32) and lo = v - hi (exact in fp32);
@@ -48,8 +49,7 @@ constexpr int BKR = 16;  // K chunk (rows) of the MN-major kernel
 // ------------------------------------------------------------- tcgen05 PTX --
 // Shared-memory matrix descriptor (sm_100 format: start >> 4 at [0,14),
 // LBO >> 4 at [16,30), SBO >> 4 at [32,46), version 1 at [46,48), layout type
-// at [61,64): 2 = 128-byte swizzle, 1 = 128-byte swizzle on 32-byte atoms).
-constexpr uint32_t kLayoutSW128 = 2;
+// at [61,64): 4 = 64-byte swizzle, 1 = 128-byte swizzle on 32-byte atoms).
 constexpr uint32_t kLayoutSW64 = 4;
 constexpr uint32_t kLayoutSW128Base32B = 1;
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
@@ -138,7 +138,8 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
                  : "memory");
 }
 
-// Split fp32 values in place into tf32 hi (kept in `hi`) and lo (to `lo`).
+// Split fp32 values in place into tf32 hi (low 13 mantissa bits cleared) and
+// lo = v - hi.
 __device__ __forceinline__ void split_tf32(float4 *hi, float4 *lo, int count, int t, int nt) {
     for (int e = t; e < count; e += nt) {
         float4 v = hi[e];
@@ -155,19 +156,22 @@ __device__ __forceinline__ void split_tf32(float4 *hi, float4 *lo, int count, in
 // ------------------------------------------------- K-major GEMM (Y = A B^T) --
 template <int D>
 struct KMajorSmem {
-    static constexpr int A_BYTES = BM * BK * 4;                // 16 KB
-    static constexpr int B_BYTES = D * BK * 4;                 // 32 KB at D = 256
+    static constexpr int A_BYTES = BM * BK * 4;                // 8 KB
+    static constexpr int B_BYTES = D * BK * 4;                 // 16 KB at D = 256
     static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;    // hi + lo of both
     static constexpr int NSTAGE = 4;
-    static constexpr int BYTES = 1024 + NSTAGE * STAGE + 256;
+    // epilogue staging: 4 warps x 2 buffers of 32 rows x 32 floats (128B swizzle)
+    static constexpr int OUT_BUF = 32 * 32 * 4;
+    static constexpr int OUT_BYTES = 4 * 2 * OUT_BUF;
+    static constexpr int BYTES = 1024 + NSTAGE * STAGE + OUT_BYTES + 256;
     static constexpr int TMEM_COLS = (2 * D <= 256) ? 256 : 512;
 };
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kmajor_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mBhi,
-                       const __grid_constant__ CUtensorMap mBlo, float *__restrict__ Y,
-                       int64_t rows, int num_tiles, int *err) {
+                       const __grid_constant__ CUtensorMap mBlo, const __grid_constant__ CUtensorMap mY,
+                       int num_tiles, int *err) {
     using S = KMajorSmem<D>;
     constexpr int NK = D / BK;
     extern __shared__ unsigned char smem_raw[];
@@ -175,7 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
     unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     unsigned char *stage0 = base;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + S::NSTAGE * S::STAGE);
+    unsigned char *outbuf = stage0 + S::NSTAGE * S::STAGE;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(outbuf + S::OUT_BYTES);
     constexpr int NS = S::NSTAGE;
     uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS,
              *accempty = bars + 3 * NS + 2;
@@ -200,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&mA);
         prefetch_tensormap(&mBhi);
         prefetch_tensormap(&mBlo);
+        prefetch_tensormap(&mY);
     }
     if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
     tc_fence_before();
@@ -274,28 +280,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
+        // Each warp drains its 32 TMEM lanes (rows) in 32-column chunks into a
+        // 128B-swizzled 32x32 staging buffer (lane = row; the swizzle spreads
+        // the 8 float4 of a row over all banks) and one lane TMA-stores it.
+        // The tensor map clips rows past the end of the batch.
         const int q = warp & 3;  // TMEM lane quarter of this warp
+        unsigned char *mybuf = outbuf + q * 2 * S::OUT_BUF;
+        int chunk = 0;
         for (int lt = 0; lt < my_tiles && ok; ++lt) {
             const int tile = blockIdx.x + lt * gridDim.x;
             const int b = lt & 1;
             if (!(ok = mbar_wait_bounded(&accfull[b], (lt >> 1) & 1, err, 0x205))) break;
             tc_fence_after();
-            const int64_t row = (int64_t)tile * BM + q * 32 + lane;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * D;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < D / 32; ++c, ++chunk) {
                 float v[32];
                 tmem_ld32(taddr + c * 32, v);
-                if (row < rows) {
-                    float4 *dst = reinterpret_cast<float4 *>(Y + row * D + c * 32);
+                if (c == D / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(&accempty[b]);
+                }
+                unsigned char *buf = mybuf + (chunk & 1) * S::OUT_BUF;
+                if (lane == 0) bulk_wait_read<1>();
+                __syncwarp();
+                float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 128);
 #pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                for (int u = 0; u < 8; ++u)
+                    rowp[u ^ (lane & 7)] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&mY, buf, c * 32, tile * BM + q * 32);
+                    bulk_commit();
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&accempty[b]);
         }
+        if (lane == 0) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
@@ -533,8 +554,9 @@ int launch_kmajor(const float *A, const float *Bhi, const float *Blo, float *Y, 
     if (st) return st;
     int *err = nullptr;
     if ((st = device_error_word(&err))) return st;
-    CUtensorMap mA, mBh, mBl;
+    CUtensorMap mA, mBh, mBl, mY;
     const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    if ((st = make_tmap_2d(&mY, Y, D, rows, D * 4, 32, 32))) return st;
     if ((st = make_tmap_2d(&mA, A, D, rows, D * 4, BK, BM, sw))) return st;
     if ((st = make_tmap_2d(&mBh, Bhi, D, D, D * 4, BK, D, sw))) return st;
     if ((st = make_tmap_2d(&mBl, Blo, D, D, D * 4, BK, D, sw))) return st;
@@ -543,12 +565,12 @@ int launch_kmajor(const float *A, const float *Bhi, const float *Blo, float *Y, 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_kmajor)");
     const int64_t tiles = (rows + BM - 1) / BM;
-    if (tiles > (1 << 30)) {
+    if (rows >= ((int64_t)1 << 31)) {  // TMA row coordinates are 32-bit signed
         set_error("layer: batch too large");
         return CB_ERR_UNSUPPORTED;
     }
     const int grid = (int)std::min<int64_t>(tiles, di.sm_count);
-    kern<<<grid, kThreads, S::BYTES, s>>>(mA, mBh, mBl, Y, rows, (int)tiles, err);
+    kern<<<grid, kThreads, S::BYTES, s>>>(mA, mBh, mBl, mY, (int)tiles, err);
     e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gemm_kmajor_kernel");
 }
