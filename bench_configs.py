@@ -37,7 +37,12 @@ except Exception:
     pass
 HBM_GBS = float(PEAKS.get("hbm_gbs", 6650.0))
 BF16_TFLOPS = float(PEAKS.get("bf16_tflops", 1590.0))
-TF32_TFLOPS = BF16_TFLOPS / 2       # dense tf32 issues at half the bf16 rate
+SM_MAX_MHZ = float(PEAKS.get("sm_max_mhz", 1965.0))
+# Nominal tcgen05 kind::tf32 rate at the maximum SM clock: one 128x256x8 MMA
+# per 128 cycles per SM = 4096 FLOP/clk/SM (cliffordcuda_b200/csrc/
+# probe_mma_rate.cu measures this per-clock rate). Higher, i.e. stricter, than
+# measured bf16 / 2, which carries cuBLAS's efficiency and the power cap.
+TF32_TFLOPS = 148 * 4096 * SM_MAX_MHZ * 1e6 / 1e12
 X3TF32_TFLOPS = TF32_TFLOPS / 3     # three tf32 MMAs per fp32-accurate product
 
 
@@ -168,7 +173,10 @@ def layer(args, world, rank, dev, T):
     r = res["gp"]
     roof = {"bound": "tensor", "achieved": r["useful_tflops"], "peak": X3TF32_TFLOPS,
             "unit": "TFLOP/s", "frac": r["frac_3xtf32_peak"], "traffic": None,
-            "peak_source": "measured bf16 dense / 2 (tf32) / 3 (3xTF32 MMAs per product)",
+            "peak_source": "nominal tf32 tensor rate at max SM clock (148 SMs x 4096 FLOP/clk, "
+                           "per-clock rate measured by probe_mma_rate) / 3 (3xTF32 MMAs "
+                           "per product)",
+            "frac_of_measured_bf16_over_6": r["useful_tflops"] / (BF16_TFLOPS / 6),
             "tensor_issue_tflops": 3 * r["useful_tflops"], "tf32_peak": TF32_TFLOPS}
     return _line(args, world, "Cl(8,0) GeometricProductLayer training rows/s",
                  r["rows_per_s"], "rows/s", ms, clk, cfg,

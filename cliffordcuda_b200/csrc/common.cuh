@@ -107,6 +107,46 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase,
     return ok != 0;
 }
 
+// As mbar_try_wait, with acquire at cluster scope: for barriers that threads
+// of another CTA in the cluster arrive on (their prior writes become visible).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t phase,
+                                                      uint32_t hint_ns = 20000) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Arrive on the barrier at the same shared offset as `bar` in CTA `rank` of
+// this cluster (the own CTA included). Default (CTA-scope release)
+// semantics: a cluster-scope release costs a cluster-wide memory barrier on
+// every arrival. Writers of shared data that an async-proxy reader consumes
+// fence the proxy (fence.proxy.async) before arriving.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t *bar, uint32_t rank) {
+    asm volatile(
+        "{\n\t.reg .b32 ra;\n\t"
+        "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+        "mbarrier.arrive.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+        "r"(rank)
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Full barrier over all threads of all CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -118,10 +158,12 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // false (the caller then stops issuing work; nothing traps).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, int *err,
                                                   int code,
-                                                  uint64_t timeout_ns = 2000000000ull) {
-    if (mbar_try_wait(bar, phase)) return true;
+                                                  uint64_t timeout_ns = 2000000000ull,
+                                                  bool cluster = false) {
+    auto poll = [&] { return cluster ? mbar_try_wait_cluster(bar, phase) : mbar_try_wait(bar, phase); };
+    if (poll()) return true;
     const uint64_t t0 = global_timer_ns();
-    while (!mbar_try_wait(bar, phase)) {
+    while (!poll()) {
         if (global_timer_ns() - t0 > timeout_ns) {
             atomicCAS(err, 0, code);
             return false;

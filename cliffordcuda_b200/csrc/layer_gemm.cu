@@ -13,18 +13,22 @@
 //
 // GEMMs (D = 128 or 256):
 //   * gemm_kmajor_kernel: Y[rows][D] = A[rows][D] B^T with B given as [N][K]
-//     (Y = X M uses B = M^T, dX = dY M^T uses B = M). One CTA per SM,
-//     128-row tiles, K in 16-float chunks (64-byte swizzle rows), four-stage
-//     TMA pipeline, two TMEM accumulators so the epilogue of one tile
-//     overlaps the MMAs of the next.
+//     (Y = X M uses B = M^T, dX = dY M^T uses B = M). Persistent CTA pairs
+//     (cluster of 2, tcgen05 cta_group::2, M = 256): each CTA of a pair holds
+//     128 rows of the 256-row tile and half of B's N rows, so B streams from
+//     L2 once per 256 rows. K in 16-float chunks (64-byte swizzle rows),
+//     six-stage TMA pipeline (eight at D = 128), two TMEM accumulators so the
+//     epilogue of one tile overlaps the MMAs of the next.
 //   * gemm_mn_kernel: G[D][D] = X^T dY with K = rows, split over CTAs; both
 //     operands are MN-major in shared memory (128-byte swizzle on 32-byte
 //     atoms, the layout the tf32 MMA requires for MN-major operands); each
 //     CTA writes a D x D partial.
 // Warp roles: warp 0 issues TMA loads, warp 1 allocates TMEM and issues the
-// MMAs (one lane), warps 2-3 split each landed A/B tile into tf32 hi and lo
-// parts in place, warps 4-7 drain TMEM (tcgen05.ld) through 128B-swizzled
-// shared staging buffers and TMA-store 32x32 chunks of Y.
+// MMAs (one lane; in the K-major kernel only in the even CTA of the pair),
+// warps 2-3 split each landed A tile (both tiles in the MN kernel) into tf32
+// hi and lo parts in place, warps 4-7 drain TMEM (tcgen05.ld); the K-major
+// kernel stages 32x32 chunks of Y in 128B-swizzled shared buffers and
+// TMA-stores them.
 //
 // 3xTF32: every operand v is split as hi = v with the low 13 mantissa bits
 // cleared (exactly representable in tf32) and lo = v - hi (exact in fp32);
@@ -138,6 +142,37 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
                  : "memory");
 }
 
+// CTA-pair (cta_group::2) forms. TMEM is allocated and freed by one warp of
+// each CTA of the pair together; the MMA is issued by one thread of the even
+// CTA; the commit arrives on the barrier at the same offset in both CTAs.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
 // Split fp32 values in place into tf32 hi (low 13 mantissa bits cleared) and
 // lo = v - hi.
 __device__ __forceinline__ void split_tf32(float4 *hi, float4 *lo, int count, int t, int nt) {
@@ -154,12 +189,22 @@ __device__ __forceinline__ void split_tf32(float4 *hi, float4 *lo, int count, in
 }
 
 // ------------------------------------------------- K-major GEMM (Y = A B^T) --
+// Runs on CTA pairs (clusters of 2, tcgen05 cta_group::2). A pair owns
+// 256-row tiles: CTA r loads rows 128r..128r+127 of the tile and rows
+// (D/2)r..(D/2)r+D/2-1 of B (the N rows of B^T), so B streams from L2 once per
+// 256 output rows and each SM's tensor core reads only half of B from its own
+// shared memory. The even CTA issues M = 256 MMAs that read both CTAs' tiles
+// and write each CTA's 128 accumulator rows into that CTA's TMEM.
+// Barriers: full (local TMA bytes), conv (in the even CTA: one arrival per
+// converter warp of both CTAs), empty and accfull (in both CTAs, signalled by
+// a multicast tcgen05.commit), accempty (in the even CTA: one arrival per
+// epilogue warp of both CTAs).
 template <int D>
 struct KMajorSmem {
-    static constexpr int A_BYTES = BM * BK * 4;                // 8 KB
-    static constexpr int B_BYTES = D * BK * 4;                 // 16 KB at D = 256
+    static constexpr int A_BYTES = BM * BK * 4;                // 8 KB (128 rows)
+    static constexpr int B_BYTES = (D / 2) * BK * 4;           // 8 KB at D = 256
     static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;    // hi + lo of both
-    static constexpr int NSTAGE = 4;
+    static constexpr int NSTAGE = D == 256 ? 6 : 8;
     // epilogue staging: 4 warps x 2 buffers of 32 rows x 32 floats (128B swizzle)
     static constexpr int OUT_BUF = 32 * 32 * 4;
     static constexpr int OUT_BYTES = 4 * 2 * OUT_BUF;
@@ -168,20 +213,21 @@ struct KMajorSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_kmajor_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mBhi,
                        const __grid_constant__ CUtensorMap mBlo, const __grid_constant__ CUtensorMap mY,
                        int num_tiles, int *err) {
     using S = KMajorSmem<D>;
     constexpr int NK = D / BK;
+    constexpr int NS = S::NSTAGE;
     extern __shared__ unsigned char smem_raw[];
     // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
+    // Both CTAs of a pair get the same layout, which the pair MMA relies on.
     unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     unsigned char *stage0 = base;
-    unsigned char *outbuf = stage0 + S::NSTAGE * S::STAGE;
+    unsigned char *outbuf = stage0 + NS * S::STAGE;
     uint64_t *bars = reinterpret_cast<uint64_t *>(outbuf + S::OUT_BYTES);
-    constexpr int NS = S::NSTAGE;
     uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS,
              *accempty = bars + 3 * NS + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * NS + 4);
@@ -191,15 +237,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto Blo = [&](int s) { return stage0 + s * S::STAGE + 2 * S::A_BYTES + S::B_BYTES; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&conv[s], 64);
+            mbar_init(&conv[s], 4);  // converter warps of both CTAs
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accfull[b], 1);
-            mbar_init(&accempty[b], 128);
+            mbar_init(&accempty[b], 8);  // epilogue warps of both CTAs
         }
         fence_barrier_init();
         prefetch_tensormap(&mA);
@@ -207,63 +255,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&mBlo);
         prefetch_tensormap(&mY);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+    if (warp == 1) tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int my_tiles = (num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int my_tiles = (num_tiles - pair + npairs - 1) / npairs;
     bool ok = true;
 
     if (warp == 0) {
         if (lane == 0) {
             int it = 0;
             for (int lt = 0; lt < my_tiles && ok; ++lt) {
-                const int tile = blockIdx.x + lt * gridDim.x;
+                const int tile = pair + lt * npairs;
                 for (int kc = 0; kc < NK && ok; ++kc, ++it) {
                     const int s = it % NS;
                     if (!(ok = mbar_wait_bounded(&empty[s], ((it / NS) + 1) & 1, err, 0x201))) break;
                     mbar_arrive_expect_tx(&full[s], S::A_BYTES + 2 * S::B_BYTES);
-                    tma_load_2d(Ahi(s), &mA, kc * BK, tile * BM, &full[s]);
-                    tma_load_2d(Bhi(s), &mBhi, kc * BK, 0, &full[s]);
-                    tma_load_2d(Blo(s), &mBlo, kc * BK, 0, &full[s]);
+                    tma_load_2d(Ahi(s), &mA, kc * BK, tile * (2 * BM) + (int)rank * BM, &full[s]);
+                    tma_load_2d(Bhi(s), &mBhi, kc * BK, (int)rank * (D / 2), &full[s]);
+                    tma_load_2d(Blo(s), &mBlo, kc * BK, (int)rank * (D / 2), &full[s]);
                 }
             }
+            // The last commits arrive on this CTA's empty barriers from the
+            // even CTA; take them before the CTA may exit.
+            for (int j = it - NS < 0 ? 0 : it - NS; j < it && ok; ++j)
+                ok = mbar_wait_bounded(&empty[j % NS], (j / NS) & 1, err, 0x206);
         }
     } else if (warp == 1) {
-        constexpr uint32_t idesc = idesc_tf32(BM, D, false, false);
-        int it = 0;
-        for (int lt = 0; lt < my_tiles && ok; ++lt) {
-            const int b = lt & 1;
-            if (lane == 0) ok = mbar_wait_bounded(&accempty[b], ((lt >> 1) + 1) & 1, err, 0x202);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t dcol = tmem + b * D;
-            for (int kc = 0; kc < NK && ok; ++kc, ++it) {
-                const int s = it % NS;
-                if (lane == 0) ok = mbar_wait_bounded(&conv[s], (it / NS) & 1, err, 0x203);
+        if (leader) {
+            constexpr uint32_t idesc = idesc_tf32(2 * BM, D, false, false);
+            int it = 0;
+            for (int lt = 0; lt < my_tiles && ok; ++lt) {
+                const int b = lt & 1;
+                if (lane == 0)
+                    ok = mbar_wait_bounded(&accempty[b], ((lt >> 1) + 1) & 1, err, 0x202,
+                                           2000000000ull, true);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t ah = smem_u32(Ahi(s)), al = smem_u32(Alo(s));
-                    const uint32_t bh = smem_u32(Bhi(s)), bl = smem_u32(Blo(s));
+                const uint32_t dcol = tmem + b * D;
+                for (int kc = 0; kc < NK && ok; ++kc, ++it) {
+                    const int s = it % NS;
+                    if (lane == 0)
+                        ok = mbar_wait_bounded(&conv[s], (it / NS) & 1, err, 0x203, 2000000000ull, true);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t ah = smem_u32(Ahi(s)), al = smem_u32(Alo(s));
+                        const uint32_t bh = smem_u32(Bhi(s)), bl = smem_u32(Blo(s));
 #pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        const uint32_t off = kk * 32;  // 8 fp32 along K within a 64-byte row
-                        const uint64_t dah = kmajor_desc(ah + off);
-                        const uint64_t dal = kmajor_desc(al + off);
-                        const uint64_t dbh = kmajor_desc(bh + off);
-                        const uint64_t dbl = kmajor_desc(bl + off);
-                        mma_tf32(dcol, dah, dbh, idesc, (kc | kk) ? 1u : 0u);
-                        mma_tf32(dcol, dah, dbl, idesc, 1u);
-                        mma_tf32(dcol, dal, dbh, idesc, 1u);
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            const uint32_t off = kk * 32;  // 8 fp32 along K within a 64-byte row
+                            const uint64_t dah = kmajor_desc(ah + off);
+                            const uint64_t dal = kmajor_desc(al + off);
+                            const uint64_t dbh = kmajor_desc(bh + off);
+                            const uint64_t dbl = kmajor_desc(bl + off);
+                            mma_tf32_pair(dcol, dah, dbh, idesc, (kc | kk) ? 1u : 0u);
+                            mma_tf32_pair(dcol, dah, dbl, idesc, 1u);
+                            mma_tf32_pair(dcol, dal, dbh, idesc, 1u);
+                        }
+                        mma_commit_pair(&empty[s]);
+                        if (kc == NK - 1) mma_commit_pair(&accfull[b]);
                     }
-                    mma_commit(&empty[s]);
-                    if (kc == NK - 1) mma_commit(&accfull[b]);
+                    __syncwarp();
                 }
-                __syncwarp();
             }
         }
     } else if (warp < 4) {
@@ -276,7 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 split_tf32(reinterpret_cast<float4 *>(Ahi(s)), reinterpret_cast<float4 *>(Alo(s)),
                            S::A_BYTES / 16, t, 64);
                 fence_proxy_async_smem();
-                mbar_arrive(&conv[s]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(&conv[s], 0);
             }
         }
     } else {
@@ -288,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         unsigned char *mybuf = outbuf + q * 2 * S::OUT_BUF;
         int chunk = 0;
         for (int lt = 0; lt < my_tiles && ok; ++lt) {
-            const int tile = blockIdx.x + lt * gridDim.x;
+            const int tile = pair + lt * npairs;
             const int b = lt & 1;
             if (!(ok = mbar_wait_bounded(&accfull[b], (lt >> 1) & 1, err, 0x205))) break;
             tc_fence_after();
@@ -299,7 +358,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld32(taddr + c * 32, v);
                 if (c == D / 32 - 1) {
                     tc_fence_before();
-                    mbar_arrive(&accempty[b]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(&accempty[b], 0);
                 }
                 unsigned char *buf = mybuf + (chunk & 1) * S::OUT_BUF;
                 if (lane == 0) bulk_wait_read<1>();
@@ -311,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&mY, buf, c * 32, tile * BM + q * 32);
+                    tma_store_2d(&mY, buf, c * 32, tile * (2 * BM) + (int)rank * BM + q * 32);
                     bulk_commit();
                 }
             }
@@ -319,9 +379,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) bulk_wait_all();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // no MMA of the pair still reads this CTA's tiles or TMEM
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, S::TMEM_COLS);
+    if (warp == 1) tmem_dealloc_pair(tmem, S::TMEM_COLS);
 }
 
 // ------------------------------------------ MN-major GEMM (G = X^T dY, split-K) --
@@ -558,18 +618,34 @@ int launch_kmajor(const float *A, const float *Bhi, const float *Blo, float *Y, 
     const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
     if ((st = make_tmap_2d(&mY, Y, D, rows, D * 4, 32, 32))) return st;
     if ((st = make_tmap_2d(&mA, A, D, rows, D * 4, BK, BM, sw))) return st;
-    if ((st = make_tmap_2d(&mBh, Bhi, D, D, D * 4, BK, D, sw))) return st;
-    if ((st = make_tmap_2d(&mBl, Blo, D, D, D * 4, BK, D, sw))) return st;
+    if ((st = make_tmap_2d(&mBh, Bhi, D, D, D * 4, BK, D / 2, sw))) return st;
+    if ((st = make_tmap_2d(&mBl, Blo, D, D, D * 4, BK, D / 2, sw))) return st;
     using S = KMajorSmem<D>;
     auto kern = gemm_kmajor_kernel<D>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_kmajor)");
-    const int64_t tiles = (rows + BM - 1) / BM;
+    const int64_t tiles = (rows + 2 * BM - 1) / (2 * BM);  // 256-row pair tiles
     if (rows >= ((int64_t)1 << 31)) {  // TMA row coordinates are 32-bit signed
         set_error("layer: batch too large");
         return CB_ERR_UNSUPPORTED;
     }
-    const int grid = (int)std::min<int64_t>(tiles, di.sm_count);
+    static int max_pairs[64] = {};  // per device: co-resident CTA pairs
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int &mp = max_pairs[dev & 63];
+    if (mp == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (di.sm_count / 2));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = S::BYTES;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = di.sm_count / 2;
+        }
+        mp = n;
+    }
+    const int grid = 2 * (int)std::min<int64_t>(tiles, mp);
     kern<<<grid, kThreads, S::BYTES, s>>>(mA, mBh, mBl, mY, (int)tiles, err);
     e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gemm_kmajor_kernel");
