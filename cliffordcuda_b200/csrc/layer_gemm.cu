@@ -19,7 +19,8 @@
 //     L2 once per 256 rows. K in 16-float chunks (64-byte swizzle rows),
 //     six-stage TMA pipeline (eight at D = 128), two TMEM accumulators so the
 //     epilogue of one tile overlaps the MMAs of the next.
-//   * gemm_mn_kernel: G[D][D] = X^T dY with K = rows, split over CTAs; both
+//   * gemm_mn_kernel: G[D][D] = X^T dY with K = rows, split over CTAs (CTA
+//     pairs at D = 256, gemm_mn_pair_kernel); both
 //     operands are MN-major in shared memory (128-byte swizzle on 32-byte
 //     atoms, the layout the tf32 MMA requires for MN-major operands); each
 //     CTA writes a D x D partial.
@@ -590,6 +591,167 @@ int check_layer(int op, int n, uint32_t neg, uint32_t zero) {
     return CB_OK;
 }
 
+// CTA-pair form of the MN-major kernel for D = 256 (tcgen05 cta_group::2,
+// M = 256): both CTAs of a pair read the same rows; CTA r loads features
+// 128r..128r+127 of X (its half of M) and of dY (its half of N), so each SM
+// splits and feeds the tensor core half of every operand chunk. Converters
+// write only lo = v - hi next to the raw values, which serve as hi: the tf32
+// MMA reads the top 19 bits of each fp32 operand (sign, exponent, 10 mantissa
+// bits) and ignores the rest, so the raw value is read as exactly
+// hi = v & 0xFFFFE000. The fp32-accuracy tests of the layer and rotor
+// backward passes fail if that does not hold. CTA r's TMEM holds rows
+// 128r..128r+127 of the pair's D x D partial.
+struct MNPairSmem {
+    static constexpr int HALF = 128;                    // features per CTA
+    static constexpr int OP_BYTES = HALF * BKR * 4;     // 8 KB
+    static constexpr int STAGE = 4 * OP_BYTES;          // X raw, X lo, dY raw, dY lo
+    static constexpr int NSTAGE = 6;
+    static constexpr int BYTES = 1024 + NSTAGE * STAGE + 256;
+    static constexpr int TMEM_COLS = 256;
+    static constexpr int CONV_WARPS = 6;                // warps 2-7
+};
+
+// lo = v - (v with the low 13 mantissa bits cleared), v read from `raw`.
+__device__ __forceinline__ void split_lo(const float4 *raw, float4 *lo, int count, int t, int nt) {
+    for (int e = t; e < count; e += nt) {
+        const float4 v = raw[e];
+        lo[e] = make_float4(v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                            v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                            v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                            v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+    }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_mn_pair_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mG,
+                        float *__restrict__ partial, int64_t rows, int64_t rows_per_part, int *err) {
+    using S = MNPairSmem;
+    constexpr int D = 256;
+    constexpr int NS = S::NSTAGE;
+    extern __shared__ unsigned char smem_raw[];
+    // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
+    // the compiler keeps the shared address space; identical in both CTAs.
+    unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    unsigned char *stage0 = base;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + NS * S::STAGE);
+    uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * NS + 1);
+    auto op = [&](int s, int which) { return stage0 + s * S::STAGE + which * S::OP_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int part = blockIdx.x >> 1;
+    const int64_t r0 = (int64_t)part * rows_per_part;
+    const int64_t r1 = std::min<int64_t>(rows, r0 + rows_per_part);
+    const int nchunks = r1 > r0 ? (int)((r1 - r0 + BKR - 1) / BKR) : 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 2 * S::CONV_WARPS);  // converter warps of both CTAs
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accfull, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&mX);
+        prefetch_tensormap(&mG);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const int f0 = (int)rank * S::HALF;
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int s = c % NS;
+                if (!(ok = mbar_wait_bounded(&empty[s], ((c / NS) + 1) & 1, err, 0x221))) break;
+                mbar_arrive_expect_tx(&full[s], 2 * S::OP_BYTES);
+                const int row = (int)(r0 + (int64_t)c * BKR);
+                for (int g = 0; g < S::HALF / 32; ++g) {
+                    tma_load_2d(op(s, 0) + g * MN_BOX_BYTES, &mX, f0 + g * 32, row, &full[s]);
+                    tma_load_2d(op(s, 2) + g * MN_BOX_BYTES, &mG, f0 + g * 32, row, &full[s]);
+                }
+            }
+            // The last commits arrive on this CTA's empty barriers from the
+            // even CTA; take them before the CTA may exit.
+            for (int j = nchunks - NS < 0 ? 0 : nchunks - NS; j < nchunks && ok; ++j)
+                ok = mbar_wait_bounded(&empty[j % NS], (j / NS) & 1, err, 0x226);
+        }
+    } else if (warp == 1) {
+        if (leader) {
+            constexpr uint32_t idesc = idesc_tf32(2 * BM, D, true, true);
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int s = c % NS;
+                if (lane == 0)
+                    ok = mbar_wait_bounded(&conv[s], (c / NS) & 1, err, 0x222, 2000000000ull, true);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t xh = smem_u32(op(s, 0)), xl = smem_u32(op(s, 1));
+                    const uint32_t gh = smem_u32(op(s, 2)), gl = smem_u32(op(s, 3));
+#pragma unroll
+                    for (int kk = 0; kk < BKR / 8; ++kk) {
+                        const uint32_t koff = kk * 1024;  // next 8 rows of K
+                        const uint64_t dxh = mnmajor_desc(xh + koff, MN_BOX_BYTES);
+                        const uint64_t dxl = mnmajor_desc(xl + koff, MN_BOX_BYTES);
+                        const uint64_t dgh = mnmajor_desc(gh + koff, MN_BOX_BYTES);
+                        const uint64_t dgl = mnmajor_desc(gl + koff, MN_BOX_BYTES);
+                        mma_tf32_pair(tmem, dxh, dgh, idesc, (c | kk) ? 1u : 0u);
+                        mma_tf32_pair(tmem, dxh, dgl, idesc, 1u);
+                        mma_tf32_pair(tmem, dxl, dgh, idesc, 1u);
+                    }
+                    mma_commit_pair(&empty[s]);
+                    if (c == nchunks - 1) mma_commit_pair(accfull);
+                }
+                __syncwarp();
+            }
+        }
+    } else {
+        const int t = threadIdx.x - 64;
+        for (int c = 0; c < nchunks && ok; ++c) {
+            const int s = c % NS;
+            if (!(ok = mbar_wait_bounded(&full[s], (c / NS) & 1, err, 0x223))) break;
+            split_lo(reinterpret_cast<const float4 *>(op(s, 0)), reinterpret_cast<float4 *>(op(s, 1)),
+                     S::OP_BYTES / 16, t, 32 * S::CONV_WARPS);
+            split_lo(reinterpret_cast<const float4 *>(op(s, 2)), reinterpret_cast<float4 *>(op(s, 3)),
+                     S::OP_BYTES / 16, t, 32 * S::CONV_WARPS);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(&conv[s], 0);
+        }
+        if (warp >= 4) {  // epilogue: TMEM lane quarter warp % 4
+            const int q = warp & 3;
+            const int i = (int)rank * S::HALF + q * 32 + lane;
+            float *dst0 = partial + (size_t)part * D * D + (size_t)i * D;
+            if (nchunks > 0 && ok && (ok = mbar_wait_bounded(accfull, 0, err, 0x224))) {
+                tc_fence_after();
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(taddr + c * 32, v);
+                    float4 *dst = reinterpret_cast<float4 *>(dst0 + c * 32);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                }
+            } else if (nchunks == 0) {
+                for (int k = 0; k < D; ++k) dst0[k] = 0.0f;
+            }
+        }
+    }
+    tc_fence_before();
+    cluster_sync();  // no MMA of the pair still reads this CTA's tiles or TMEM
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem, S::TMEM_COLS);
+}
+
+
 // Split of the batch for G = X^T dY: about 512 rows per partial keeps the
 // fp32 accumulation in TMEM short (the partials are summed in double), at
 // most 8 partials per SM.
@@ -662,13 +824,21 @@ int launch_mn(const float *x, const float *dy, float *partial, int64_t batch, in
         return st;
     if ((st = make_tmap_2d(&mG, dy, D, batch, D * 4, 32, BKR, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)))
         return st;
-    auto kern = gemm_mn_kernel<D>;
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MNSmem<D>::BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_mn)");
     const int64_t chunks = (batch + BKR - 1) / BKR;
-    const int64_t rows_per_cta = ((chunks + parts - 1) / parts) * BKR;
-    kern<<<parts, kThreads, MNSmem<D>::BYTES, s>>>(mX, mG, partial, batch, rows_per_cta, err);
+    const int64_t rows_per_part = ((chunks + parts - 1) / parts) * BKR;
+    cudaError_t e;
+    if constexpr (D == 256) {  // one CTA pair per partial
+        e = cudaFuncSetAttribute(gemm_mn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 MNPairSmem::BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_mn_pair)");
+        gemm_mn_pair_kernel<<<2 * parts, kThreads, MNPairSmem::BYTES, s>>>(mX, mG, partial, batch,
+                                                                             rows_per_part, err);
+    } else {
+        auto kern = gemm_mn_kernel<D>;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MNSmem<D>::BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_mn)");
+        kern<<<parts, kThreads, MNSmem<D>::BYTES, s>>>(mX, mG, partial, batch, rows_per_part, err);
+    }
     e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gemm_mn_kernel");
 }

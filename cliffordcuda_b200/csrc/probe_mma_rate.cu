@@ -6,8 +6,11 @@
 // the tensor core's tf32 rate per clock: one 128 x 256 x 8 MMA per 128 cycles
 // per SM, i.e. 4096 FLOP/clk/SM.
 //
-//   make -C cliffordcuda_b200/csrc probe && cliffordcuda_b200/csrc/_build/probe_mma_rate
+//   make -C cliffordcuda_b200/csrc probe && cliffordcuda_b200/csrc/_build/probe_mma_rate [seconds]
+// With `seconds`, it also reports the rate over that long a run of
+// back-to-back launches (the sustained rate under the power cap).
 #include <cstdio>
+#include <cstdlib>
 #include <cstdint>
 #include "common.cuh"
 using namespace cb;
@@ -95,7 +98,34 @@ void run(int iters, int *err, unsigned long long *cyc) {
     double macs = 148.0 * 128 * N * 8 * 6.0 * iters;  // per SM: 128 rows x N x K=8, 6 MMAs per iter
     printf("pair=%d N=%d: %.3f ms  %.1f TFLOP/s tf32  err=%d cuda=%d cyc/iter=%.1f\n", PAIR, N, ms, 2 * macs / ms / 1e9, h, (int)e, (double)c0 / iters);
 }
-int main() {
+// Back-to-back launches for about `seconds` (the power cap settles the clock):
+// average rate over the loop.
+template <int PAIR, int N>
+void sustained(double seconds, int iters, int *err, unsigned long long *cyc) {
+    auto f = k<PAIR, N>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(148); cfg.blockDim = dim3(128); cfg.dynamicSmemBytes = 65536 + 1024;
+    cudaLaunchAttribute at[1]; at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = PAIR ? 2 : 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+    cfg.attrs = at; cfg.numAttrs = 1;
+    cudaEvent_t e0, e1; cudaEventCreate(&e0); cudaEventCreate(&e1);
+    cudaLaunchKernelEx(&cfg, f, iters, err, cyc);
+    cudaEventRecord(e0);
+    cudaLaunchKernelEx(&cfg, f, iters, err, cyc);
+    cudaEventRecord(e1);
+    cudaEventSynchronize(e1);
+    float ms1; cudaEventElapsedTime(&ms1, e0, e1);
+    const int reps = (int)(seconds * 1e3 / ms1) + 1;
+    cudaEventRecord(e0);
+    for (int r = 0; r < reps; ++r) cudaLaunchKernelEx(&cfg, f, iters, err, cyc);
+    cudaEventRecord(e1);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms; cudaEventElapsedTime(&ms, e0, e1);
+    double macs = 148.0 * 128 * N * 8 * 6.0 * iters * reps;
+    printf("sustained pair=%d N=%d: %d launches in %.1f ms  %.1f TFLOP/s tf32  cuda=%d\n", PAIR, N, reps, ms, 2 * macs / ms / 1e9, (int)e);
+}
+int main(int argc, char **argv) {
+    const double seconds = argc > 1 ? atof(argv[1]) : 0.0;
     int *err; unsigned long long *cyc;
     cudaMalloc(&err, 4); cudaMemset(err, 0, 4); cudaMalloc(&cyc, 148 * 8);
     run<0, 256>(4000, err, cyc);
@@ -103,5 +133,6 @@ int main() {
     run<0, 128>(4000, err, cyc);
     run<1, 128>(4000, err, cyc);
     run<0, 256>(4000, err, cyc);
+    if (seconds > 0) sustained<0, 256>(seconds, 4000, err, cyc);
     return 0;
 }

@@ -12,10 +12,11 @@
 // (rows I and columns J in increasing generator order). The metric is not used,
 // as in the reference. This file evaluates that map directly:
 //
-//   compile:  one CTA in fp64 -- Rm by scaling and squaring of a Taylor series
+//   compile:  fp64 -- Rm by scaling and squaring of a Taylor series
 //             (||B / 2^s||_1 <= 1/8, 20 terms), then every equal-grade minor
 //             C_k[I][J] = det(Rm[I, J]) by Gaussian elimination with partial
-//             pivoting. Per grade k the C(n,k) x C(n,k) matrix is stored
+//             pivoting, spread over CTAs that each recompute Rm. Per grade
+//             k the C(n,k) x C(n,k) matrix is stored
 //             row-major, grades concatenated (C(2n, n) entries in total).
 //   apply:    y = x C_full with C_full the D x D matrix holding every C_k at
 //             its blades' (bit-pattern) positions and zeros between grades;
@@ -28,7 +29,8 @@
 //             double). The no-allocation variant instead runs a fused
 //             CUDA-core pass (dx and per-CTA partial sums of dC) over a fixed
 //             in-library array. The chain to the
-//             bivector runs in one CTA in fp64:
+//             bivector runs in one 1024-thread CTA in fp64 (one warp per
+//             entry of dRm, no atomics):
 //               dRm[p][q] = sum_{I, J} dC[I][J] (-1)^(a+b) det(Rm[I\p, J\q])
 //             (a, b = positions of p in I and q in J; the cofactors are the
 //             grade k-1 minors already computed), then the adjoint Frechet
@@ -224,6 +226,9 @@ __device__ double minor_det(int n, const double *Rm, uint32_t I, uint32_t J, int
 }
 
 // State (fp64) layout: Bm [n*n], Rm [n*n], C64 [total].
+// Each CTA computes Rm = expm(B) itself (a few microseconds at n <= 10) and
+// then the minors e = blockIdx.x * 256 + threadIdx.x, ... of its slice; CTA 0
+// also stores B and Rm.
 __global__ void __launch_bounds__(256)
     rotor_compile_kernel(const float *__restrict__ beta, int n, float *__restrict__ cs,
                          double *__restrict__ state) {
@@ -243,13 +248,15 @@ __global__ void __launch_bounds__(256)
             }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < nn; e += blockDim.x) state[e] = Bm[e];  // B (unscaled)
+    if (blockIdx.x == 0)
+        for (int e = threadIdx.x; e < nn; e += blockDim.x) state[e] = Bm[e];  // B (unscaled)
     __syncthreads();
     expm(n, Bm, Rm, T, W);
-    for (int e = threadIdx.x; e < nn; e += blockDim.x) state[nn + e] = Rm[e];
+    if (blockIdx.x == 0)
+        for (int e = threadIdx.x; e < nn; e += blockDim.x) state[nn + e] = Rm[e];
     build_blade_tables(L, rank, blades);
     double *C64 = state + 2 * nn;
-    for (int e = threadIdx.x; e < L.total; e += blockDim.x) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < L.total; e += gridDim.x * blockDim.x) {
         int k = 0;
         while (e >= L.coff[k + 1]) ++k;
         const int ck = L.ck[k];
@@ -449,8 +456,17 @@ __global__ void rotor_reduce_kernel(const float *__restrict__ partial, int parts
     dcs[e] = s;
 }
 
-// dcs -> dbeta (one CTA, fp64).
-__global__ void __launch_bounds__(256)
+// dcs -> dbeta (one CTA of 1024 threads, fp64).
+// dRm[p][q] = sum over grades k >= 1 and blades I containing p, J containing q
+// (|I| = |J| = k) of (-1)^(a+b) dC_k[I][J] det Rm[I \ p, J \ q], a and b the
+// positions of p in I and of q in J: the cofactor expansion of d det / d Rm.
+// One warp per entry (p, q): lane t takes the subsets I' of the other n - 1
+// generators numbered t, t + 32, ... and pairs each with every J' of the same
+// size; the grade k - 1 minor det Rm[I', J'] is C_{k-1} from the forward pass.
+// The adjoint Frechet derivative is linear in dRm, so dRm enters the block
+// exponential divided by a power of two near its largest entry (exact), which
+// keeps the number of squarings set by B alone, and the result is scaled back.
+__global__ void __launch_bounds__(1024)
     rotor_compile_bwd_kernel(const double *__restrict__ state, const float *__restrict__ dcs,
                              int n, float *__restrict__ dbeta) {
     const Layout L = make_layout(n);
@@ -458,36 +474,41 @@ __global__ void __launch_bounds__(256)
     __shared__ double dRm[kMaxN * kMaxN];
     __shared__ double Z[4 * kMaxN * kMaxN], E[4 * kMaxN * kMaxN], T[4 * kMaxN * kMaxN],
         W[4 * kMaxN * kMaxN];
-    __shared__ int rank[1 << kMaxN], blades[1 << kMaxN];
-    build_blade_tables(L, rank, blades);
+    __shared__ int rank[1 << kMaxN];
+    __shared__ double dscale;
     const double *Bm = state;
     const double *C64 = state + 2 * nn;
-    for (int e = threadIdx.x; e < nn; e += blockDim.x) dRm[e] = 0.0;
+    for (int bp = threadIdx.x; bp < L.D; bp += blockDim.x) rank[bp] = blade_rank(bp);
     __syncthreads();
-    for (int e = threadIdx.x; e < L.total; e += blockDim.x) {
-        int k = 0;
-        while (e >= L.coff[k + 1]) ++k;
-        if (k == 0) continue;
-        const double v = (double)dcs[e];
-        if (v == 0.0) continue;
-        const int ck = L.ck[k], ck1 = L.ck[k - 1];
-        const uint32_t I = blades[L.goff[k] + (e - L.coff[k]) / ck];
-        const uint32_t J = blades[L.goff[k] + (e - L.coff[k]) % ck];
-        int a = 0;
-        for (int p = 0; p < n; ++p) {
-            if (!((I >> p) & 1u)) continue;
-            const uint32_t Ip = I & ~(1u << p);
-            int b = 0;
-            for (int q = 0; q < n; ++q) {
-                if (!((J >> q) & 1u)) continue;
-                const uint32_t Jq = J & ~(1u << q);
-                const double minor =
-                    (k == 1) ? 1.0 : C64[L.coff[k - 1] + rank[Ip] * ck1 + rank[Jq]];
-                atomicAdd(&dRm[p * n + q], ((a + b) & 1) ? -v * minor : v * minor);
-                ++b;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint32_t sub = 1u << (n - 1);
+    for (int e = warp; e < nn; e += nwarps) {
+        const int p = e / n, q = e % n;
+        const uint32_t lowp = (1u << p) - 1, lowq = (1u << q) - 1;
+        double acc = 0.0;
+        for (uint32_t i = lane; i < sub; i += 32) {
+            const uint32_t Ip = (i & lowp) | ((i & ~lowp) << 1);  // I' (skips generator p)
+            const int k1 = __popc(i), k = k1 + 1;
+            const int ck = L.ck[k], ck1 = L.ck[k1];
+            const int a = __popc(Ip & lowp);
+            const uint32_t I = Ip | (1u << p);
+            const int rowI = L.coff[k] + rank[I] * ck, rowIp = L.coff[k1] + rank[Ip] * ck1;
+            for (uint32_t j = 0; j < sub; ++j) {
+                if (__popc(j) != k1) continue;
+                const uint32_t Jp = (j & lowq) | ((j & ~lowq) << 1);
+                const uint32_t J = Jp | (1u << q);
+                const double t = (double)__ldg(&dcs[rowI + rank[J]]) * __ldg(&C64[rowIp + rank[Jp]]);
+                acc += ((a + __popc(Jp & lowq)) & 1) ? -t : t;
             }
-            ++a;
         }
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) dRm[e] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double mx = 0.0;
+        for (int e = 0; e < nn; ++e) mx = fmax(mx, fabs(dRm[e]));
+        dscale = mx > 0.0 ? ldexp(1.0, ilogb(mx) + 1) : 1.0;
     }
     __syncthreads();
     // Z = [[B^T, dRm], [0, B^T]]
@@ -496,7 +517,7 @@ __global__ void __launch_bounds__(256)
         double v = 0.0;
         if (i < n && j < n) v = Bm[j * n + i];
         else if (i >= n && j >= n) v = Bm[(j - n) * n + (i - n)];
-        else if (i < n && j >= n) v = dRm[i * n + (j - n)];
+        else if (i < n && j >= n) v = dRm[i * n + (j - n)] / dscale;
         Z[e] = v;
     }
     __syncthreads();
@@ -506,7 +527,7 @@ __global__ void __launch_bounds__(256)
         for (int p = 0; p < n - 1; ++p)
             for (int q = p + 1; q < n; ++q, ++idx) {
                 const double dpq = E[p * m + n + q], dqp = E[q * m + n + p];
-                dbeta[idx] = (float)(2.0 * (dpq - dqp));
+                dbeta[idx] = (float)(2.0 * (dpq - dqp) * dscale);
             }
     }
 }
@@ -570,7 +591,8 @@ extern "C" int cb_rotor_compile(const float *beta, int n, float *cs, double *sta
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    rotor_compile_kernel<<<1, 256, 0, s>>>(beta, n, cs, state);
+    const int cgrid = std::min((make_layout(n).total + 255) / 256, 2 * di.sm_count);
+    rotor_compile_kernel<<<cgrid, 256, 0, s>>>(beta, n, cs, state);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "launch rotor_compile_kernel");
     const Layout L = make_layout(n);
@@ -694,7 +716,7 @@ extern "C" int cb_rotor_compile_bwd(const double *state, const float *dcs, int n
     }
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    rotor_compile_bwd_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(state, dcs, n, dbeta);
+    rotor_compile_bwd_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(state, dcs, n, dbeta);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_compile_bwd_kernel");
 }

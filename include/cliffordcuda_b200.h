@@ -122,7 +122,7 @@ CB_API int cb_layer_backward(int op, const float *mats, const float *x, const fl
 CB_API int cb_rotor_sizes(int n, int64_t *cs_floats, int64_t *state_doubles);
 
 /*
- * beta (1, n(n-1)/2) lex-pair bivector -> cs, state. One CTA, fp64.
+ * beta (1, n(n-1)/2) lex-pair bivector -> cs, state. fp64.
  * Replaces eigh_exp_fwd (kernels/rotor/eigh_exp.cu:270-322) followed by
  * givens_factor_fwd_v2 (kernels/rotor/givens_factor.cu:7-59, :233-238).
  */
