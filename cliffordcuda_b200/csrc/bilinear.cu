@@ -170,6 +170,7 @@ int bilinear(int op, int mode, const float *x, const float *y, float *out, int64
              uint32_t neg, uint32_t zero, cudaStream_t stream) {
     int st = check_args(op, mode, x, y, out, batch, n, neg, zero);
     if (st || batch == 0) return st;
+    if (use_mat16(op, n, neg, zero, x, y, out)) return gp_mat16(mode, x, y, out, batch, stream);
     if (use_tiled(op, n, neg, zero, x, y, out, batch)) {
         switch (mode) {
         case CB_MODE_FWD:

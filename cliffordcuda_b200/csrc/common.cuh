@@ -241,6 +241,12 @@ int gemm3x_mn(int D, const float *X, const float *dY, float *partial, int64_t ro
 int reduce_partials(const float *partial, int parts, int DD, float *G, cudaStream_t s);
 int split_mats(const float *M, float *mats, int D, cudaStream_t s);
 
+// Cl(8,0) geometric product through the 16 x 16 real matrix representation
+// (gp_mat16.cu): applicable when use_mat16 holds; mode as in cb_bilinear.
+bool use_mat16(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
+               const void *o);
+int gp_mat16(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s);
+
 // internal bilinear dispatcher (bilinear.cu)
 int bilinear(int op, int mode, const float *x, const float *y, float *out, int64_t batch, int n,
              uint32_t neg, uint32_t zero, cudaStream_t stream);

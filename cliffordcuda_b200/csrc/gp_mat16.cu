@@ -1,0 +1,374 @@
+// gp_mat16.cu -- the geometric product of Cl(8,0) and both of its backward
+// sums through the real 16 x 16 matrix representation of the algebra.
+//
+// Cl(8,0) is isomorphic to the algebra of real 16 x 16 matrices. With 16 x 16
+// generator matrices G_i (G_i^2 = 1, G_i G_j = -G_j G_i) the blade e_I maps to
+// E_I = G_i1 G_i2 ... (i1 < i2 < ...), a signed permutation matrix, and the
+// map rho(a) = sum_I a_I E_I turns the geometric product into a matrix
+// product: rho(a * b) = rho(a) rho(b). The E_I are orthogonal with
+// <E_I, E_J>_F = 16 delta_IJ, so rho / 4 is an isometry and the backward sums
+// of the reference's autograd (grad_a = d<g, a*b>/da, grad_b = d<g, a*b>/db,
+// reference extensions/ga/geom_prod.py:241-250) are
+//     grad_a = rho^-1(rho(g) rho(b)^T),   grad_b = rho^-1(rho(a)^T rho(g)).
+// Per product that is one 16 x 16 x 16 matrix product (4096 FMA) plus the
+// basis changes, against 65,536 FMA per sum for the blade-by-blade sum; the
+// kernel is bound by HBM instead of the FP32 pipe.
+//
+// Generators: tensor products of four real 2 x 2 Pauli factors
+//   I, X = [[0,1],[1,0]], Z = [[1,0],[0,-1]], W = XZ = [[0,-1],[1,0]]
+// (W^2 = -1), G_0 = I(x)I(x)I(x)X, G_1 = I(x)I(x)I(x)Z, and
+// G_{2+i} = P_i (x) W with P_0..P_5 six mutually anticommuting 3-factor
+// strings that square to -1 (kP below). A product of such strings is +-one
+// string, so the coefficient vector of rho(a) in the string basis is a signed
+// permutation of a, and the change from string coefficients to matrix entries
+// factorises over the four factors into 2-term butterflies:
+//   per factor, (c_I, c_Z) -> (m_00, m_11) = (c_I + c_Z, c_I - c_Z) and
+//               (c_X, c_W) -> (m_01, m_10) = (c_X - c_W, c_X + c_W).
+//
+// Work split: a warp handles 8 products, 4 lanes each. Lane q of a product
+// holds the 64 string coefficients whose last factor has code q; factors 1-3
+// are transformed in registers, factor 4 by one shuffle with lane q ^ 2,
+// after which lane q holds one 8 x 8 quadrant of the matrix (row parity
+// q >> 1, column parity (q >> 1) ^ (q & 1)). Lanes store their quadrants to
+// shared memory in the layout the product reads, each lane computes its
+// quadrant of the 16 x 16 product by 16 outer-product steps, and the inverse
+// transform runs the same way back. Rows come in and go out by bulk copies
+// (1 KB each) into padded per-product regions of shared memory; each warp is
+// its own CTA with one buffer.
+#include <algorithm>
+#include <utility>
+
+#include "common.cuh"
+
+namespace cb {
+namespace {
+
+// Real Pauli factor codes: I = 0, X = 1, Z = 2, W = 3 (bit 0: off-diagonal,
+// bit 1: the Z part); the code of a product is the XOR of the codes.
+__host__ __device__ constexpr int pauli_sign(int a, int b) {
+    // a * b = pauli_sign(a, b) * (a ^ b)
+    return (a == 2 && (b == 1 || b == 3)) || (a == 3 && (b == 1 || b == 3)) ? -1 : 1;
+}
+
+// P_0 .. P_5: codes of factors 1, 2, 3.
+__host__ __device__ constexpr int kP(int i, int f) {
+    constexpr int t[6][3] = {{0, 0, 3}, {0, 3, 1}, {1, 3, 2}, {2, 3, 2}, {3, 0, 2}, {3, 1, 1}};
+    return t[i][f];
+}
+
+__host__ __device__ constexpr int popc8(int v) {
+    int c = 0;
+    for (int b = 0; b < 8; ++b) c += (v >> b) & 1;
+    return c;
+}
+
+// Blade bits 2..7 (k, generators G_2..G_7): the register slot of the
+// factor-1..3 string of E_I (codes of factors 1, 2, 3 at bits 4-5, 2-3, 0-1)
+// and the sign of the ordered product P_i1 P_i2 ... relative to that string.
+__host__ __device__ constexpr int slot_of(int k) {
+    int c[3] = {0, 0, 0};
+    for (int i = 0; i < 6; ++i)
+        if ((k >> i) & 1)
+            for (int f = 0; f < 3; ++f) c[f] ^= kP(i, f);
+    return c[0] << 4 | c[1] << 2 | c[2];
+}
+__host__ __device__ constexpr int sig1_of(int k) {
+    int c[3] = {0, 0, 0}, s = 1;
+    for (int i = 0; i < 6; ++i)
+        if ((k >> i) & 1)
+            for (int f = 0; f < 3; ++f) {
+                s *= pauli_sign(c[f], kP(i, f));
+                c[f] ^= kP(i, f);
+            }
+    return s;
+}
+
+// Last factor of E_I: X^I0 Z^I1 W^m (m = popcount of blade bits 2..7) equals
+// sign * (code q) with q = (I0 ^ m&1) | (I1 ^ m&1) << 1; the sign for lane q.
+__host__ __device__ constexpr int last_sign(int q, int m) {
+    const int pi = m & 1, i0 = (q & 1) ^ pi, i1 = ((q >> 1) & 1) ^ pi;
+    int c = 0, s = 1;
+    if (i0) { s *= pauli_sign(c, 1); c ^= 1; }
+    if (i1) { s *= pauli_sign(c, 2); c ^= 2; }
+    for (int t = 0; t < m; ++t) { s *= pauli_sign(c, 3); c ^= 3; }
+    return s;
+}
+
+// Quadrant entry (i, j) (row 2i + r4, column 2j + c4) -> register slot:
+// per factor f the code d | r << 1 with r = row bit, d = row bit ^ column bit.
+__host__ __device__ constexpr int slot_ij(int i, int j) {
+    const int d = i ^ j;
+    int s = 0;
+    for (int f = 0; f < 3; ++f) {
+        const int r = (i >> (2 - f)) & 1, df = (d >> (2 - f)) & 1;
+        s |= (df | r << 1) << (4 - 2 * f);
+    }
+    return s;
+}
+
+// Per product a 1168-byte region (292 floats, 16 bytes past a multiple of
+// 128): it holds the padded input row (lane gathers then hit 32 distinct
+// banks), then the matrix as four 8 x 8 blocks 288 bytes apart (a quarter
+// warp's 128-bit stores and the product's 128-bit reads then hit distinct
+// banks), then the output row.
+constexpr int kRowFloats = 292;
+constexpr int kBlockFloats = 72;
+constexpr int kRegion = 8 * kRowFloats;      // 8 products
+constexpr int kBufFloats = 2 * kRegion;      // U and V
+constexpr int kSmemBytes = kBufFloats * 4 + 64;
+
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_store(void *gdst, const void *smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_u32(smem_src)), "r"(bytes)
+                 : "memory");
+}
+
+// r[slot(k)] = sign(E_I) * lane factor * row[I] for all 64 k, where the
+// blade I of register k in lane q has bits 2..7 = k and bits 0..1 = q, or
+// q ^ 3 when k has odd parity (the W factors of G_2..G_7 also carry the
+// last-factor code).
+template <int K>
+__device__ __forceinline__ void gather1(float (&r)[64], const float *row, int qx0, int qx3,
+                                        const float (&S)[4]) {
+    constexpr int m = popc8(K);
+    const float v = row[4 * K + ((m & 1) ? qx3 : qx0)] * S[m & 3];
+    r[slot_of(K)] = sig1_of(K) > 0 ? v : -v;
+}
+template <int... K>
+__device__ __forceinline__ void gather(float (&r)[64], const float *row, int q, const float (&S)[4],
+                                       std::integer_sequence<int, K...>) {
+    (gather1<K>(r, row, q, q ^ 3, S), ...);
+}
+template <int K>
+__device__ __forceinline__ void scatter1(const float (&r)[64], float *row, int qx0, int qx3,
+                                         const float (&S)[4]) {
+    constexpr int m = popc8(K);
+    const float v = r[slot_of(K)] * S[m & 3];
+    row[4 * K + ((m & 1) ? qx3 : qx0)] = sig1_of(K) > 0 ? v : -v;
+}
+template <int... K>
+__device__ __forceinline__ void scatter(const float (&r)[64], float *row, int q, const float (&S)[4],
+                                        std::integer_sequence<int, K...>) {
+    (scatter1<K>(r, row, q, q ^ 3, S), ...);
+}
+
+// String coefficients -> matrix entries over factors 1-3 (in registers).
+__device__ __forceinline__ void to_matrix3(float (&r)[64]) {
+#pragma unroll
+    for (int f = 0; f < 3; ++f) {
+        const int tb = 5 - 2 * f, sb = 4 - 2 * f;
+#pragma unroll
+        for (int s = 0; s < 64; ++s) {
+            if ((s >> tb) & 1) continue;
+            const float p0 = r[s], p1 = r[s | 1 << tb];
+            if ((s >> sb) & 1) {
+                r[s] = p0 - p1;
+                r[s | 1 << tb] = p0 + p1;
+            } else {
+                r[s] = p0 + p1;
+                r[s | 1 << tb] = p0 - p1;
+            }
+        }
+    }
+}
+// Matrix entries -> string coefficients over factors 1-3 (times 2 per factor).
+__device__ __forceinline__ void from_matrix3(float (&r)[64]) {
+#pragma unroll
+    for (int f = 0; f < 3; ++f) {
+        const int tb = 5 - 2 * f, sb = 4 - 2 * f;
+#pragma unroll
+        for (int s = 0; s < 64; ++s) {
+            if ((s >> tb) & 1) continue;
+            const float m0 = r[s], m1 = r[s | 1 << tb];
+            r[s] = m0 + m1;
+            r[s | 1 << tb] = ((s >> sb) & 1) ? m1 - m0 : m0 - m1;
+        }
+    }
+}
+// Factor 4 across the lane pair (q, q ^ 2): r += c * partner's r.
+__device__ __forceinline__ void factor4(float (&r)[64], float c) {
+#pragma unroll
+    for (int s = 0; s < 64; ++s) r[s] = fmaf(c, __shfl_xor_sync(0xffffffffu, r[s], 2), r[s]);
+}
+
+// Store this lane's quadrant (row parity a, column parity b) into the matrix
+// layout the product reads: block (row parity, column parity) of 64 floats;
+// the A operand column-major within a block (columns of A contiguous), the B
+// operand row-major. TRANS stores the transpose (block and entry swapped).
+template <bool A_OPERAND, bool TRANS>
+__device__ __forceinline__ void store_quadrant(float *mat, int a, int b, const float (&r)[64]) {
+    const int blk = TRANS ? b * 2 + a : a * 2 + b;
+    float *base = mat + blk * kBlockFloats;
+    // entry (i, j) of the quadrant goes to base + (J_MAJOR ? j * 8 + i : i * 8 + j)
+    constexpr bool J_MAJOR = A_OPERAND != TRANS;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 v;
+            if (J_MAJOR)  // u = j, consecutive i
+                v = make_float4(r[slot_ij(4 * h + 0, u)], r[slot_ij(4 * h + 1, u)],
+                                r[slot_ij(4 * h + 2, u)], r[slot_ij(4 * h + 3, u)]);
+            else  // u = i, consecutive j
+                v = make_float4(r[slot_ij(u, 4 * h + 0)], r[slot_ij(u, 4 * h + 1)],
+                                r[slot_ij(u, 4 * h + 2)], r[slot_ij(u, 4 * h + 3)]);
+            *reinterpret_cast<float4 *>(base + u * 8 + 4 * h) = v;
+        }
+}
+
+// acc(i, j) = sum_k A[(i, r4)][k] B[k][(j, c4)] for this lane's quadrant.
+__device__ __forceinline__ void quadrant_product(float (&acc)[64], const float *A, const float *B,
+                                                 int r4, int c4) {
+#pragma unroll
+    for (int s = 0; s < 64; ++s) acc[s] = 0.0f;
+#pragma unroll
+    for (int k4 = 0; k4 < 2; ++k4)
+#pragma unroll 2
+        for (int kp = 0; kp < 8; ++kp) {
+            const float4 *pa =
+                reinterpret_cast<const float4 *>(A + (r4 * 2 + k4) * kBlockFloats + kp * 8);
+            const float4 *pb =
+                reinterpret_cast<const float4 *>(B + (k4 * 2 + c4) * kBlockFloats + kp * 8);
+            const float4 a0 = pa[0], a1 = pa[1], b0 = pb[0], b1 = pb[1];
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[slot_ij(i, j)] = fmaf(av[i], bv[j], acc[slot_ij(i, j)]);
+        }
+}
+
+// out = rho^-1(op(U) op(V)): FWD U = x, V = y; GRAD_A (x = b, y = g) U = g,
+// V = b transposed; GRAD_B (x = a, y = g) U = a transposed, V = g.
+// One buffer per warp; the load latency of one warp's batch is hidden by the
+// other warps of the SM (12 per SM; a second, prefetching buffer per warp
+// halves that count and measured 20% slower).
+template <int MODE>
+__global__ void __launch_bounds__(32)
+    gp_mat16_kernel(const float *__restrict__ x, const float *__restrict__ y,
+                    float *__restrict__ out, int64_t batch, int64_t nbatches, int *err) {
+    constexpr bool SWAP = MODE == CB_MODE_GRAD_A;
+    constexpr bool TU = MODE == CB_MODE_GRAD_B, TV = MODE == CB_MODE_GRAD_A;
+    const float *gu = SWAP ? y : x;
+    const float *gv = SWAP ? x : y;
+    extern __shared__ __align__(16) float sm[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + kBufFloats);
+    const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
+    const int r4 = q >> 1, c4 = r4 ^ (q & 1);
+    if (lane == 0) {
+        mbar_init(full, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    // Lane factors: sign of the last string factor for each m mod 4, with the
+    // factor-4 butterfly's lane sign folded in (forward: -1 on lane 2; inverse:
+    // -1 on lane 2 and the 1/16 of the three in-register and one shuffled
+    // half-steps).
+    float s_in[4], s_out[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const float s = (float)last_sign(q, m);
+        s_in[m] = q == 2 ? -s : s;
+        s_out[m] = (q == 2 ? -s : s) * 0.0625f;
+    }
+    const float c_fwd = r4 ? 1.0f : -1.0f;  // factor 4, forward
+    const float c_inv = r4 ? -1.0f : 1.0f;  // factor 4, inverse
+
+    bool ok = true;
+    int64_t bt = blockIdx.x;
+    for (int it = 0; bt < nbatches && ok; bt += gridDim.x, ++it) {
+        const int64_t r0 = bt * 8;
+        const int nv = (int)std::min<int64_t>(8, batch - r0);
+        if (lane == 0) {
+            bulk_wait_read<0>();  // the previous batch's store has read the buffer
+            mbar_arrive_expect_tx(full, (uint32_t)nv * 2048u);
+            for (int i = 0; i < nv; ++i) {
+                bulk_load(sm + i * kRowFloats, gu + (r0 + i) * 256, 1024, full);
+                bulk_load(sm + kRegion + i * kRowFloats, gv + (r0 + i) * 256, 1024, full);
+            }
+        }
+        ok = mbar_wait_bounded(full, it & 1, err, 0x301);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        float *U = sm + p * kRowFloats;
+        float *V = U + kRegion;
+        float r[64];
+        gather(r, U, q, s_in, std::make_integer_sequence<int, 64>{});
+        __syncwarp();  // every lane of the product has read its U row
+        to_matrix3(r);
+        factor4(r, c_fwd);
+        store_quadrant<true, TU>(U, r4, c4, r);
+        gather(r, V, q, s_in, std::make_integer_sequence<int, 64>{});
+        __syncwarp();
+        to_matrix3(r);
+        factor4(r, c_fwd);
+        store_quadrant<false, TV>(V, r4, c4, r);
+        __syncwarp();
+        quadrant_product(r, U, V, r4, c4);
+        __syncwarp();  // all reads of the matrices done before U is overwritten
+        factor4(r, c_inv);
+        from_matrix3(r);
+        scatter(r, U, q, s_out, std::make_integer_sequence<int, 64>{});
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            for (int i = 0; i < nv; ++i) bulk_store(out + (r0 + i) * 256, sm + i * kRowFloats, 1024);
+            bulk_commit();
+        }
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+template <int MODE>
+int launch_mat16(const float *x, const float *y, float *out, int64_t batch, cudaStream_t s) {
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    int *err = nullptr;
+    if ((st = device_error_word(&err))) return st;
+    auto kern = gp_mat16_kernel<MODE>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gp_mat16)");
+    static int per_sm[3] = {0, 0, 0};
+    int &ps = per_sm[MODE];
+    if (ps == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, kern, 32, kSmemBytes) != cudaSuccess ||
+            ps < 1) {
+            cudaGetLastError();
+            ps = 1;
+        }
+    }
+    const int64_t nb = (batch + 7) / 8;
+    const int grid = (int)std::min<int64_t>(nb, (int64_t)ps * di.sm_count);
+    kern<<<grid, 32, kSmemBytes, s>>>(x, y, out, batch, nb, err);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_mat16_kernel");
+}
+
+}  // namespace
+
+bool use_mat16(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
+               const void *o) {
+    if (op != CB_OP_GP || n != 8 || neg || zero) return false;
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    return al(x) && al(y) && al(o);
+}
+
+int gp_mat16(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s) {
+    if (batch == 0) return CB_OK;
+    switch (mode) {
+    case CB_MODE_FWD: return launch_mat16<CB_MODE_FWD>(x, y, out, batch, s);
+    case CB_MODE_GRAD_A: return launch_mat16<CB_MODE_GRAD_A>(x, y, out, batch, s);
+    default: return launch_mat16<CB_MODE_GRAD_B>(x, y, out, batch, s);
+    }
+}
+
+}  // namespace cb
