@@ -37,11 +37,12 @@ UNIT = "products/s"
 NNZ_GP = 4 ** N_GEN                   # non-zeros of the Cl(8,0) sign table
 FLOPS_PER_SUM = 2 * NNZ_GP            # one FMA per non-zero term
 BYTES_PER_SUM = 3 * D * 4             # two operand rows read, one row written
-# DRAM bytes per row of one gp_mat16_kernel launch, from ncu: dram__bytes_read.sum
+BYTES_PER_BWD = 5 * D * 4             # a, b, g read; grad_a, grad_b written
+# DRAM bytes per row of one gp_mat16_bwd_kernel launch, from ncu: dram__bytes_read.sum
 # + dram__bytes_write.sum of a 262,144-row launch / rows (profiles/gp_mat16_cl8.md:
-# (537.0 + 235.2) MB / 262,144). Every row is read once and written once, so the
+# (805.6 + 496.3) MB / 262,144). Every row is read once and written once, so the
 # per-launch traffic is this times the batch.
-MEASURED_TRAFFIC_PER_SUM = (537.0e6 + 235.2e6) / 262144
+MEASURED_TRAFFIC_PER_BWD = (805.6e6 + 496.3e6) / 262144
 
 
 def hbm_peak_gbs():
@@ -214,7 +215,7 @@ def main():
 
     import cliffordcuda_b200 as cc
     from cliffordcuda_b200 import _lib
-    from cliffordcuda_b200.products import bilinear_raw
+    from cliffordcuda_b200.products import bilinear_raw, bilinear_bwd_raw
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -233,13 +234,17 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     def step(events=None):
-        calls = (("fwd", a, b, c), ("grad_a", b, g, ga), ("grad_b", a, g, gb))
-        for i, (mode, x, y, o) in enumerate(calls):
-            if events is not None:
-                events[i][0].record(stream)
-            bilinear_raw("gp", mode, x, y, N_GEN, metric, out=o)
-            if events is not None:
-                events[i][1].record(stream)
+        # forward, then both backward sums in one call: the two native calls
+        # the public API's autograd makes (cb_bilinear, cb_bilinear_bwd)
+        if events is not None:
+            events[0][0].record(stream)
+        bilinear_raw("gp", "fwd", a, b, N_GEN, metric, out=c)
+        if events is not None:
+            events[0][1].record(stream)
+            events[1][0].record(stream)
+        bilinear_bwd_raw("gp", a, b, g, N_GEN, metric, ga, gb)
+        if events is not None:
+            events[1][1].record(stream)
 
     def barrier():
         if world > 1:
@@ -251,7 +256,7 @@ def main():
     _lib.device_status(dev)
 
     K = args.steps
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(3)]
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(2)]
           for _ in range(K)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -264,21 +269,23 @@ def main():
         torch.cuda.synchronize(dev)
     barrier()
     ms = t_start.elapsed_time(t_end)
-    launch_ms = [e[0].elapsed_time(e[1]) for s in ev for e in s]
+    fwd_ms = statistics.mean(s[0][0].elapsed_time(s[0][1]) for s in ev)
+    bwd_ms = statistics.mean(s[1][0].elapsed_time(s[1][1]) for s in ev)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = t.item()
     _lib.device_status(dev)
     value = world * B * K / (ms / 1000.0)
-    kernel_ms = statistics.mean(launch_ms)
     # The Cl(8,0) geometric product runs through the 16 x 16 matrix
-    # representation (gp_mat16_kernel): about 8k FP32 operations per product
-    # and sum instead of 131k, so the kernel is HBM-bound; the roofline is
-    # the algorithmic bytes (two rows read, one written) over measured HBM.
-    achieved = BYTES_PER_SUM * B / (kernel_ms / 1000.0) / 1e9
+    # representation (gp_mat16_kernel, gp_mat16_bwd_kernel): about 8k FP32
+    # operations per product and sum instead of 131k, so the kernels are
+    # HBM-bound. The roofline is the dominant launch, the fused backward:
+    # algorithmic bytes (a, b, g read, grad_a, grad_b written) over measured HBM.
+    kernel_ms = bwd_ms
+    achieved = BYTES_PER_BWD * B / (kernel_ms / 1000.0) / 1e9
     peak, peak_src = hbm_peak_gbs()
-    eff_tflops = FLOPS_PER_SUM * B / (kernel_ms / 1000.0) / 1e12
+    eff_tflops = 3 * FLOPS_PER_SUM * B / ((fwd_ms + bwd_ms) / 1000.0) / 1e12
     fp32_peak = fp32_peak_tflops(dev)
 
     e2e_value = None
@@ -298,7 +305,7 @@ def main():
                    "kind": "port",
                    "sample": f"{rows} Cl(8,0) products fwd+bwd, fp32 torch einsum port of "
                              f"_shared/_einsum_refs.py, {threads} threads"}
-        traffic = (MEASURED_TRAFFIC_PER_SUM * B) if MEASURED_TRAFFIC_PER_SUM else None
+        traffic = (MEASURED_TRAFFIC_PER_BWD * B) if MEASURED_TRAFFIC_PER_BWD else None
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True,
@@ -308,8 +315,11 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "peak_source": peak_src,
-                         "kernel": "gp_mat16_kernel", "kernel_ms_per_launch": kernel_ms,
-                         "algorithmic_bytes_per_launch": BYTES_PER_SUM * B},
+                         "kernel": "gp_mat16_bwd_kernel", "kernel_ms_per_launch": kernel_ms,
+                         "algorithmic_bytes_per_launch": BYTES_PER_BWD * B,
+                         "fwd": {"kernel": "gp_mat16_kernel", "ms_per_launch": fwd_ms,
+                                 "gbs": BYTES_PER_SUM * B / (fwd_ms / 1000.0) / 1e9,
+                                 "frac": BYTES_PER_SUM * B / (fwd_ms / 1000.0) / 1e9 / peak}},
             "pct_fp32_peak": 100.0 * eff_tflops / fp32_peak,
             "pct_fp32_peak_note": "effective: blade-by-blade flops (2 x 4^8 per product and "
                                   "sum) over time against the nominal FP32 peak; the matrix "
@@ -321,7 +331,7 @@ def main():
                 "path": "cliffordcuda_b200.geom_prod + autograd backward, pinned host "
                         "buffers, copies inside the timed region, 8 row chunks pipelined "
                         "over copy-in / compute / copy-out streams"},
-            "gpu_launches": 3 * K,
+            "gpu_launches": 2 * K,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

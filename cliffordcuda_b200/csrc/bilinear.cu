@@ -205,6 +205,16 @@ extern "C" int cb_bilinear_bwd(int op, const float *a, const float *b, const flo
                                uint32_t neg_mask, uint32_t zero_mask, void *stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int st = CB_OK;
+    if (grad_a && grad_b && grad_a != grad_b && cb::use_mat16(op, n, neg_mask, zero_mask, a, b, g) &&
+        cb::use_mat16(op, n, neg_mask, zero_mask, grad_a, grad_b, g)) {
+        st = cb::check_args(op, CB_MODE_GRAD_A, b, g, grad_a, batch, n, neg_mask, zero_mask);
+        if (!st) st = cb::check_args(op, CB_MODE_GRAD_B, a, g, grad_b, batch, n, neg_mask, zero_mask);
+        if (!st && (grad_a == a || grad_b == b)) {
+            cb::set_error("gradient outputs must not alias an input");
+            st = CB_ERR_INVALID;
+        }
+        return st ? st : cb::gp_mat16_bwd(a, b, g, grad_a, grad_b, batch, s);
+    }
     if (grad_a)
         st = cb::bilinear(op, CB_MODE_GRAD_A, b, g, grad_a, batch, n, neg_mask, zero_mask, s);
     if (st) return st;

@@ -246,6 +246,9 @@ int split_mats(const float *M, float *mats, int D, cudaStream_t s);
 bool use_mat16(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
                const void *o);
 int gp_mat16(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s);
+// Both backward sums in one pass (grad_a and grad_b non-null and aligned).
+int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, float *gb,
+                 int64_t batch, cudaStream_t s);
 
 // internal bilinear dispatcher (bilinear.cu)
 int bilinear(int op, int mode, const float *x, const float *y, float *out, int64_t batch, int n,

@@ -74,6 +74,19 @@ def bilinear_raw(op, mode, x, y, n, metric, out=None):
     return out
 
 
+def bilinear_bwd_raw(op, a, b, g, n, metric, ga=None, gb=None):
+    """Both backward sums of product `op` (no autograd) into ga / gb; either
+    may be None to skip it. a, b, g contiguous fp32 CUDA."""
+    neg, zero = metric_masks(metric)
+    lib = _lib.load()
+    with torch.cuda.device(g.device):
+        st = lib.cb_bilinear_bwd(_lib.OPS[op], _lib.ptr(a), _lib.ptr(b), _lib.ptr(g),
+                                 _lib.ptr(ga), _lib.ptr(gb), a.shape[0], n, neg, zero,
+                                 _lib.stream_of(g))
+    _lib.check(st, f"cb_bilinear_bwd({op})")
+    return ga, gb
+
+
 class _BilinearFunc(torch.autograd.Function):
     @staticmethod
     def forward(ctx, a, b, op, n, metric):
@@ -89,13 +102,7 @@ class _BilinearFunc(torch.autograd.Function):
         ga = torch.empty_like(a) if need_a else None
         gb = torch.empty_like(b) if need_b else None
         if need_a or need_b:
-            neg, zero = metric_masks(ctx.metric)
-            lib = _lib.load()
-            with torch.cuda.device(g.device):
-                st = lib.cb_bilinear_bwd(_lib.OPS[ctx.op], _lib.ptr(a), _lib.ptr(b), _lib.ptr(g),
-                                         _lib.ptr(ga), _lib.ptr(gb), a.shape[0], ctx.n, neg, zero,
-                                         _lib.stream_of(g))
-            _lib.check(st, f"cb_bilinear_bwd({ctx.op})")
+            bilinear_bwd_raw(ctx.op, a, b, g, ctx.n, ctx.metric, ga, gb)
         return ga, gb, None, None, None
 
 
