@@ -277,15 +277,19 @@ __global__ void __launch_bounds__(32)
 // Both backward sums in one pass over a, b, g (5 KB per product instead of 6 KB
 // for two launches): grad_b = rho^-1(rho(a)^T rho(g)) first, from a stored
 // transposed as A and g as B; then grad_a = rho^-1(rho(g) rho(b)^T), reading
-// the columns of rho(g) from the same row-major copy. Three regions per warp
-// (a, b, g), each reused for a matrix and then an output row.
+// the columns of rho(g) from the same row-major copy. Each region holds an
+// input row, then a matrix, then an output row.
 __global__ void __launch_bounds__(32)
     gp_mat16_bwd_kernel(const float *__restrict__ a, const float *__restrict__ b,
                         const float *__restrict__ g, float *__restrict__ ga,
                         float *__restrict__ gb, int64_t batch, int64_t nbatches, int *err) {
     extern __shared__ __align__(16) float sm[];
-    float *const RA = sm, *const RB = sm + kRegion, *const RG = sm + 2 * kRegion;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + 3 * kRegion);
+    // Two regions: a and g are loaded together; b is loaded into a's region
+    // once grad_b (written there) has been stored. Against three regions (all
+    // rows loaded at once) this exposes a second load per batch but fits 12
+    // warps per SM instead of 8, and measured 4.5% faster.
+    float *const RA = sm, *const RG = sm + kRegion, *const RB = sm;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + 2 * kRegion);
     const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
     const int r4 = q >> 1, c4 = r4 ^ (q & 1);
     if (lane == 0) {
@@ -303,20 +307,20 @@ __global__ void __launch_bounds__(32)
     const float c_fwd = r4 ? 1.0f : -1.0f;
     const float c_inv = r4 ? -1.0f : 1.0f;
     bool ok = true;
+    uint32_t ph = 0;  // completed phases of `full`
     int64_t bt = blockIdx.x;
-    for (int it = 0; bt < nbatches && ok; bt += gridDim.x, ++it) {
+    for (; bt < nbatches && ok; bt += gridDim.x) {
         const int64_t r0 = bt * 8;
         const int nv = (int)std::min<int64_t>(8, batch - r0);
         if (lane == 0) {
             bulk_wait_read<0>();  // the previous batch's stores have read the regions
-            mbar_arrive_expect_tx(full, (uint32_t)nv * 3072u);
+            mbar_arrive_expect_tx(full, (uint32_t)nv * 2048u);
             for (int i = 0; i < nv; ++i) {
                 bulk_load(RA + i * kRowFloats, a + (r0 + i) * 256, 1024, full);
-                bulk_load(RB + i * kRowFloats, b + (r0 + i) * 256, 1024, full);
                 bulk_load(RG + i * kRowFloats, g + (r0 + i) * 256, 1024, full);
             }
         }
-        ok = mbar_wait_bounded(full, it & 1, err, 0x302);
+        ok = mbar_wait_bounded(full, ph++ & 1, err, 0x302);
         if (!__all_sync(0xffffffffu, ok)) break;
         float *A = RA + p * kRowFloats, *B = RB + p * kRowFloats, *G = RG + p * kRowFloats;
         float r[64];
@@ -342,6 +346,13 @@ __global__ void __launch_bounds__(32)
             for (int i = 0; i < nv; ++i) bulk_store(gb + (r0 + i) * 256, RA + i * kRowFloats, 1024);
             bulk_commit();
         }
+        if (lane == 0) {
+            bulk_wait_read<0>();  // grad_b has left region A
+            mbar_arrive_expect_tx(full, (uint32_t)nv * 1024u);
+            for (int i = 0; i < nv; ++i) bulk_load(RB + i * kRowFloats, b + (r0 + i) * 256, 1024, full);
+        }
+        ok = mbar_wait_bounded(full, ph++ & 1, err, 0x304);
+        if (!__all_sync(0xffffffffu, ok)) break;
         gather(r, B, q, s_in, std::make_integer_sequence<int, 64>{});
         __syncwarp();
         to_matrix3(r);
@@ -415,14 +426,13 @@ int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, floa
     if (st) return st;
     int *err = nullptr;
     if ((st = device_error_word(&err))) return st;
-    constexpr int kBwdSmem = 3 * kRegion * 4 + 64;
-    cudaError_t e = cudaFuncSetAttribute(gp_mat16_bwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+    constexpr int kBwdSmem = 2 * kRegion * 4 + 64;
+    auto kern = gp_mat16_bwd_kernel;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gp_mat16_bwd)");
     static int per_sm = 0;
     if (per_sm == 0) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gp_mat16_bwd_kernel, 32,
-                                                          kBwdSmem) != cudaSuccess ||
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32, kBwdSmem) != cudaSuccess ||
             per_sm < 1) {
             cudaGetLastError();
             per_sm = 1;
@@ -430,7 +440,7 @@ int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, floa
     }
     const int64_t nb = (batch + 7) / 8;
     const int grid = (int)std::min<int64_t>(nb, (int64_t)per_sm * di.sm_count);
-    gp_mat16_bwd_kernel<<<grid, 32, kBwdSmem, s>>>(a, b, g, ga, gb, batch, nb, err);
+    kern<<<grid, 32, kBwdSmem, s>>>(a, b, g, ga, gb, batch, nb, err);
     e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_mat16_bwd_kernel");
 }
