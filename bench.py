@@ -192,6 +192,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-blade-sum", action="store_true",
+                    help="skip timing the blade-by-blade kernels beside the headline")
     ap.add_argument("--batch", type=int, default=None,
                     help="rows per GPU (profiling runs use a smaller case)")
     ap.add_argument("--workload", default="headline",
@@ -288,6 +290,12 @@ def main():
     eff_tflops = 3 * FLOPS_PER_SUM * B / ((fwd_ms + bwd_ms) / 1000.0) / 1e12
     fp32_peak = fp32_peak_tflops(dev)
 
+    # The north-star algorithm for path (a): the blade-by-blade sum on the
+    # CUDA cores (bilinear_tiled_kernel via cb_bilinear_direct), same workload,
+    # fwd + grad_a + grad_b, timed per launch against the FP32 peak.
+    blade = blade_sum_path(a, b, g, c, ga, gb, metric, stream, dev, world, barrier,
+                           fp32_peak) if not args.no_blade_sum else None
+
     e2e_value = None
     if not args.no_e2e:
         e2e_value, host_out = run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier)
@@ -324,6 +332,7 @@ def main():
             "pct_fp32_peak_note": "effective: blade-by-blade flops (2 x 4^8 per product and "
                                   "sum) over time against the nominal FP32 peak; the matrix "
                                   "representation executes about 1/16 of those flops",
+            "blade_sum_path": blade,
             "cpu_baseline": cpu,
             "e2e": None if e2e_value is None else {
                 "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 3 * B * D * 4,
@@ -337,6 +346,46 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def blade_sum_path(a, b, g, c, ga, gb, metric, stream, dev, world, barrier, fp32_peak, K=20):
+    """Products/s and % of FP32 peak of the blade-by-blade kernels on the
+    headline workload (three launches per step, CUDA events per launch)."""
+    from cliffordcuda_b200.products import bilinear_raw
+    B = a.shape[0]
+    calls = (("fwd", a, b, c), ("grad_a", b, g, ga), ("grad_b", a, g, gb))
+
+    def step(ev=None):
+        for i, (mode, x, y, o) in enumerate(calls):
+            if ev is not None:
+                ev[i][0].record(stream)
+            bilinear_raw("gp", mode, x, y, N_GEN, metric, out=o, direct=True)
+            if ev is not None:
+                ev[i][1].record(stream)
+    for _ in range(3):
+        step()
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(3)]
+          for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0.record(stream)
+    for k in range(K):
+        step(ev[k])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    launch_ms = statistics.mean(e[0].elapsed_time(e[1]) for s in ev for e in s)
+    achieved = FLOPS_PER_SUM * B / (launch_ms / 1000.0) / 1e12
+    return {"kernel": "bilinear_tiled_kernel (cb_bilinear_direct)", "steps": K,
+            "value": world * B * K / (ms / 1000.0), "unit": UNIT, "ms_per_step": ms / K,
+            "achieved_tflops": achieved, "fp32_peak_tflops": fp32_peak,
+            "pct_fp32_peak": 100.0 * achieved / fp32_peak}
 
 
 def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier, chunks=8):

@@ -27,6 +27,7 @@ _i64, _i32, _u32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_uint32, ctypes.c_
 _f32 = ctypes.c_float
 SIGNATURES = {
     "cb_bilinear": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp]),
+    "cb_bilinear_direct": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp]),
     "cb_bilinear_bwd": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp]),
     "cb_layer_workspace_bytes": (_i32, [_i32, _i64, ctypes.POINTER(_i64)]),
     "cb_layer_prepare": (_i32, [_i32, _vp, _i32, _u32, _u32, _vp, _vp, _i64, _vp]),

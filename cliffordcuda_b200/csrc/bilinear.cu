@@ -167,10 +167,11 @@ int check_args(int op, int mode, const void *x, const void *y, const void *out, 
 }  // namespace
 
 int bilinear(int op, int mode, const float *x, const float *y, float *out, int64_t batch, int n,
-             uint32_t neg, uint32_t zero, cudaStream_t stream) {
+             uint32_t neg, uint32_t zero, cudaStream_t stream, bool direct) {
     int st = check_args(op, mode, x, y, out, batch, n, neg, zero);
     if (st || batch == 0) return st;
-    if (use_mat16(op, n, neg, zero, x, y, out)) return gp_mat16(mode, x, y, out, batch, stream);
+    if (!direct && use_mat16(op, n, neg, zero, x, y, out))
+        return gp_mat16(mode, x, y, out, batch, stream);
     if (use_tiled(op, n, neg, zero, x, y, out, batch)) {
         switch (mode) {
         case CB_MODE_FWD:
@@ -198,6 +199,13 @@ extern "C" int cb_bilinear(int op, int mode, const float *x, const float *y, flo
                            void *stream) {
     return cb::bilinear(op, mode, x, y, out, batch, n, neg_mask, zero_mask,
                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cb_bilinear_direct(int op, int mode, const float *x, const float *y, float *out,
+                                  int64_t batch, int n, uint32_t neg_mask, uint32_t zero_mask,
+                                  void *stream) {
+    return cb::bilinear(op, mode, x, y, out, batch, n, neg_mask, zero_mask,
+                        static_cast<cudaStream_t>(stream), true);
 }
 
 extern "C" int cb_bilinear_bwd(int op, const float *a, const float *b, const float *g,

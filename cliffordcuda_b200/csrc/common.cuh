@@ -251,7 +251,8 @@ int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, floa
                  int64_t batch, cudaStream_t s);
 
 // internal bilinear dispatcher (bilinear.cu)
+// direct: always the blade-by-blade kernels (never the matrix representation).
 int bilinear(int op, int mode, const float *x, const float *y, float *out, int64_t batch, int n,
-             uint32_t neg, uint32_t zero, cudaStream_t stream);
+             uint32_t neg, uint32_t zero, cudaStream_t stream, bool direct = false);
 
 }  // namespace cb

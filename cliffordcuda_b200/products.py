@@ -61,15 +61,17 @@ def _dims(a, b):
     return n
 
 
-def bilinear_raw(op, mode, x, y, n, metric, out=None):
-    """One native bilinear sum (no autograd). x, y contiguous fp32 CUDA."""
+def bilinear_raw(op, mode, x, y, n, metric, out=None, direct=False):
+    """One native bilinear sum (no autograd). x, y contiguous fp32 CUDA.
+    direct=True always uses the blade-by-blade kernels (cb_bilinear_direct)."""
     neg, zero = metric_masks(metric)
     if out is None:
         out = torch.empty_like(x)
     lib = _lib.load()
+    fn = lib.cb_bilinear_direct if direct else lib.cb_bilinear
     with torch.cuda.device(x.device):
-        st = lib.cb_bilinear(_lib.OPS[op], _lib.MODES[mode], _lib.ptr(x), _lib.ptr(y),
-                             _lib.ptr(out), x.shape[0], n, neg, zero, _lib.stream_of(x))
+        st = fn(_lib.OPS[op], _lib.MODES[mode], _lib.ptr(x), _lib.ptr(y),
+                _lib.ptr(out), x.shape[0], n, neg, zero, _lib.stream_of(x))
     _lib.check(st, f"cb_bilinear({op}, {mode})")
     return out
 

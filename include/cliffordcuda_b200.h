@@ -69,6 +69,19 @@ CB_API int cb_bilinear(int op, int mode, const float *x, const float *y, float *
                        void *stream);
 
 /*
+ * As cb_bilinear, always through the blade-by-blade sum kernels: the sum
+ * out[i ^ j] += s(i, j) x_i y_j evaluated term by term on the CUDA cores.
+ * cb_bilinear takes a faster route for the Euclidean Cl(8,0) geometric
+ * product (its real 16 x 16 matrix representation; same results to fp32
+ * rounding); this entry point keeps the term-by-term kernels reachable, for
+ * comparison and for callers that want them. Same reference interface as
+ * cb_bilinear (extensions/ga/geom_prod.py:216-250 and its siblings).
+ */
+CB_API int cb_bilinear_direct(int op, int mode, const float *x, const float *y, float *out,
+                              int64_t batch, int n, uint32_t neg_mask, uint32_t zero_mask,
+                              void *stream);
+
+/*
  * Both backward sums of product `op` for upstream gradient g:
  * grad_a = cb_bilinear(op, GRAD_A, b, g), grad_b = cb_bilinear(op, GRAD_B, a, g).
  * Replaces the pair of geom_prod_fwd calls in the autograd backward of

@@ -208,3 +208,18 @@ def test_fused_backward_rejects_aliasing():
     a, b, g = (torch.randn(16, 256, device=DEV) for _ in range(3))
     with pytest.raises(_lib.CliffordNativeError):
         bilinear_bwd_raw("gp", a, b, g, 8, (1,) * 8, a, torch.empty_like(a))
+
+
+def test_direct_path_cl8_gp():
+    """cb_bilinear_direct keeps the blade-by-blade kernels for the Euclidean
+    Cl(8,0) product: all three sums against the oracle, and against the
+    matrix-representation route of cb_bilinear."""
+    n, metric, batch = 8, (1,) * 8, 70
+    a, b, g = inputs(n, 21, batch)
+    ref = O.forward_backward("gp", n, metric, a, b, g)
+    ta, tb, tg = (torch.tensor(v, device=DEV) for v in (a, b, g))
+    for (mode, x, y), r in zip((("fwd", ta, tb), ("grad_a", tb, tg), ("grad_b", ta, tg)), ref):
+        d = bilinear_raw("gp", mode, x, y, n, metric, direct=True)
+        m = bilinear_raw("gp", mode, x, y, n, metric)
+        assert rel_l2(d.cpu().numpy(), r) <= REL_L2_TOL, mode
+        assert rel_l2(d.cpu().numpy(), m.cpu().numpy()) < 1e-6, mode
