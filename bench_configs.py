@@ -146,24 +146,34 @@ def layer(args, world, rank, dev, T):
     dy = torch.randn(B, D, device=dev, generator=gen)
     res = {}
     main = None
-    for name, cls in (("gp", cc.GeometricProductLayer), ("wedge", cc.WedgeProductLayer),
-                      ("lc", cc.LeftContractionLayer)):
-        lay = cls(cl)
+    from cliffordcuda_b200 import layer_ops
+    runs = (("gp", cc.GeometricProductLayer, None), ("wedge", cc.WedgeProductLayer, None),
+            ("lc", cc.LeftContractionLayer, None), ("gp_tensor_route", None, "gp"))
+    for name, cls, forced in runs:
+        lay = cls(cl) if cls is not None else cc.GeometricProductLayer(cl)
         with torch.no_grad():
             lay.weight.copy_(torch.randn(1, D, device=dev, generator=gen) / math.sqrt(D))
 
         def step():
             lay.weight.grad = None
             x.grad = None
-            y = lay(x)
+            if forced:  # the dense 3xTF32 tcgen05 route for the GP layer
+                y = layer_ops._LayerFn.apply(x, lay.weight, forced, n, tuple([1] * n))
+            else:
+                y = lay(x)
             y.backward(dy)
             allreduce_grads(lay)
         ms, clk = T.time(step, args.steps, args.warmup)
         useful = 3 * 2 * B * D * D
-        res[name] = {"rows_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
-                     "useful_tflops": useful / (ms / 1e3) / 1e12,
-                     "frac_3xtf32_peak": useful / (ms / 1e3) / 1e12 / X3TF32_TFLOPS,
-                     "hbm_gbs": 5 * D * 4 * B / (ms / 1e3) / 1e9}
+        matrix_route = name == "gp"
+        res[name] = {"route": "16x16 matrix representation (cb_layer_gp8_*)" if matrix_route
+                     else "3xTF32 tcgen05 GEMM (cb_layer_*)",
+                     "rows_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
+                     "hbm_gbs": 6 * D * 4 * B / (ms / 1e3) / 1e9 if matrix_route
+                     else 5 * D * 4 * B / (ms / 1e3) / 1e9}
+        if not matrix_route:
+            res[name]["useful_tflops"] = useful / (ms / 1e3) / 1e12
+            res[name]["frac_3xtf32_peak"] = useful / (ms / 1e3) / 1e12 / X3TF32_TFLOPS
         if main is None:
             main = (ms, clk)
     ms, clk = main
@@ -171,16 +181,24 @@ def layer(args, world, rank, dev, T):
            "per_gpu_batch": B, "global_batch": B * world, "dim": D, "metric": [1] * n,
            "l2": "x, dy 512 MiB each > L2", "parallelism": f"dp{world}"}
     r = res["gp"]
-    roof = {"bound": "tensor", "achieved": r["useful_tflops"], "peak": X3TF32_TFLOPS,
-            "unit": "TFLOP/s", "frac": r["frac_3xtf32_peak"], "traffic": None,
-            "peak_source": "nominal tf32 tensor rate at max SM clock (148 SMs x 4096 FLOP/clk, "
-                           "per-clock rate measured by probe_mma_rate) / 3 (3xTF32 MMAs "
-                           "per product)",
-            "frac_of_measured_bf16_over_6": r["useful_tflops"] / (BF16_TFLOPS / 6),
-            "tensor_issue_tflops": 3 * r["useful_tflops"], "tf32_peak": TF32_TFLOPS}
+    # The GP layer of Cl(8,0) runs through the 16 x 16 representation: HBM-bound,
+    # algorithmic bytes per row and step = x, y (forward) + dy, dx (dx) + x, dy (dw).
+    roof = {"bound": "hbm", "achieved": r["hbm_gbs"], "peak": HBM_GBS, "unit": "GB/s",
+            "frac": r["hbm_gbs"] / HBM_GBS, "traffic": None,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs",
+            "algorithmic_bytes_per_row": 6 * D * 4}
+    t = res["gp_tensor_route"]
+    tensor_route = {"layer": "GeometricProductLayer through cb_layer_* (3xTF32 tcgen05 GEMM)",
+                    "rows_per_s": t["rows_per_s"], "useful_tflops": t["useful_tflops"],
+                    "peak": X3TF32_TFLOPS, "frac": t["frac_3xtf32_peak"],
+                    "peak_source": "nominal tf32 tensor rate at max SM clock (148 SMs x 4096 "
+                                   "FLOP/clk, per-clock rate measured by probe_mma_rate) / 3 "
+                                   "(3xTF32 MMAs per product)",
+                    "frac_of_measured_bf16_over_6": t["useful_tflops"] / (BF16_TFLOPS / 6)}
     return _line(args, world, "Cl(8,0) GeometricProductLayer training rows/s",
                  r["rows_per_s"], "rows/s", ms, clk, cfg,
-                 {"roofline": roof, "layers": res}, scaling="strong")
+                 {"roofline": roof, "tensor_route": tensor_route, "layers": res},
+                 scaling="strong")
 
 
 def rotor(args, world, rank, dev, T):

@@ -34,6 +34,9 @@ SIGNATURES = {
     "cb_layer_forward": (_i32, [_vp, _vp, _vp, _i64, _i32, _vp]),
     "cb_layer_backward": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp,
                                  _i64, _vp]),
+    "cb_layer_gp8_prepare": (_i32, [_vp, _vp, _vp]),
+    "cb_layer_gp8_forward": (_i32, [_vp, _vp, _vp, _i64, _vp]),
+    "cb_layer_gp8_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp]),
     "cb_rotor_sizes": (_i32, [_i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
     "cb_rotor_compile": (_i32, [_vp, _i32, _vp, _vp, _vp]),
     "cb_rotor_apply": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),

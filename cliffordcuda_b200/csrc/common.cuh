@@ -246,6 +246,18 @@ int split_mats(const float *M, float *mats, int D, cudaStream_t s);
 bool use_mat16(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
                const void *o);
 int gp_mat16(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s);
+// GP layer of Cl(8,0) through the 16 x 16 representation (gp_mat16.cu):
+// gp_layer_weight writes [W | W^T] (2 x 288 floats) into mats; gp_layer_apply
+// computes out = rho^-1(rho(in) wm) for wm = mats (y) or mats + 288 (dx);
+// gp_layer_dw sums rho(x)^T rho(dy) over the batch into gp_layer_dw_parts(batch)
+// partials of 256 floats and writes dw.
+int gp_layer_weight(const float *w, float *mats, cudaStream_t s);
+int gp_layer_apply(const float *wm, const float *in, float *out, int64_t batch, cudaStream_t s);
+int gp_layer_dw_parts(int64_t batch);
+int gp_layer_dw(const float *x, const float *dy, float *dw, float *partial, int64_t batch,
+                cudaStream_t s);
+constexpr int kGpLayerWFloats = 288;
+
 // Both backward sums in one pass (grad_a and grad_b non-null and aligned).
 int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, float *gb,
                  int64_t batch, cudaStream_t s);

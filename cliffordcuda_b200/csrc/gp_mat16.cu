@@ -162,11 +162,14 @@ __device__ __forceinline__ void store_quadrant(float *mat, int a, int b, const f
 // acc(i, j) = sum_k A[(i, r4)][k] B[k][(j, c4)] for this lane's quadrant.
 // A_ROWMAJOR: A's blocks are stored row-major (the B-operand layout of the
 // same matrix) and its columns are read with 8 strided loads.
-template <bool A_ROWMAJOR = false>
+// ACCUMULATE: add to acc instead of starting from zero.
+template <bool A_ROWMAJOR = false, bool ACCUMULATE = false>
 __device__ __forceinline__ void quadrant_product(float (&acc)[64], const float *A, const float *B,
                                                  int r4, int c4) {
+    if (!ACCUMULATE) {
 #pragma unroll
-    for (int s = 0; s < 64; ++s) acc[s] = 0.0f;
+        for (int s = 0; s < 64; ++s) acc[s] = 0.0f;
+    }
 #pragma unroll
     for (int k4 = 0; k4 < 2; ++k4)
 #pragma unroll 2
@@ -374,6 +377,206 @@ __global__ void __launch_bounds__(32)
     if (lane == 0) bulk_wait_all();
 }
 
+// ------------------------------------------------ GP layer of Cl(8,0) --
+// y = x * w with one weight row for the batch (reference layers.py:43-47) is
+// rho(y) = rho(x) W with W = rho(w): per row one 16 x 16 x 16 product with a
+// fixed matrix. Backward: dx = rho^-1(rho(dy) W^T) and, rho / 4 being an
+// isometry, dw = rho^-1(sum over rows of rho(x)^T rho(dy)).
+// Weight operands (mats): W and W^T, each as the B operand in the padded
+// block layout of the shared tiles (4 blocks of kBlockFloats floats).
+constexpr int kWFloats = 4 * kBlockFloats;
+static_assert(kWFloats == kGpLayerWFloats, "weight operand size");
+
+__device__ __forceinline__ void lane_signs(int q, float (&s_in)[4], float (&s_out)[4]) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const float s = (float)last_sign(q, m);
+        s_in[m] = q == 2 ? -s : s;
+        s_out[m] = (q == 2 ? -s : s) * 0.0625f;
+    }
+}
+
+// One warp: lanes 0-3 convert w (lanes 4-31 repeat the work on the same row
+// so that the shuffles stay full-warp) and write W and W^T.
+__global__ void __launch_bounds__(32) gp_layer_weight_kernel(const float *__restrict__ w,
+                                                             float *__restrict__ mats) {
+    const int lane = threadIdx.x, q = lane & 3, r4 = q >> 1, c4 = r4 ^ (q & 1);
+    float s_in[4], s_out[4];
+    lane_signs(q, s_in, s_out);
+    float r[64];
+    gather(r, w, q, s_in, std::make_integer_sequence<int, 64>{});
+    to_matrix3(r);
+    factor4(r, r4 ? 1.0f : -1.0f);
+    if (lane < 4) {
+        store_quadrant<false, false>(mats, r4, c4, r);
+        store_quadrant<false, true>(mats + kWFloats, r4, c4, r);
+    }
+}
+
+// out = rho^-1(rho(in) wm), wm a B operand (W for y, W^T for dx).
+__global__ void __launch_bounds__(32)
+    gp_layer_apply_kernel(const float *__restrict__ in, float *__restrict__ out,
+                          const float *__restrict__ wm, int64_t batch, int64_t nbatches, int *err) {
+    extern __shared__ __align__(16) float sm[];
+    float *const WM = sm, *const RX = sm + kWFloats;
+    uint64_t *full = reinterpret_cast<uint64_t *>(RX + kRegion);
+    const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
+    const int r4 = q >> 1, c4 = r4 ^ (q & 1);
+    for (int e = lane; e < kWFloats; e += 32) WM[e] = wm[e];
+    if (lane == 0) {
+        mbar_init(full, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    float s_in[4], s_out[4];
+    lane_signs(q, s_in, s_out);
+    const float c_fwd = r4 ? 1.0f : -1.0f, c_inv = r4 ? -1.0f : 1.0f;
+    bool ok = true;
+    int64_t bt = blockIdx.x;
+    for (int it = 0; bt < nbatches && ok; bt += gridDim.x, ++it) {
+        const int64_t r0 = bt * 8;
+        const int nv = (int)std::min<int64_t>(8, batch - r0);
+        if (lane == 0) {
+            bulk_wait_read<0>();
+            mbar_arrive_expect_tx(full, (uint32_t)nv * 1024u);
+            for (int i = 0; i < nv; ++i) bulk_load(RX + i * kRowFloats, in + (r0 + i) * 256, 1024, full);
+        }
+        ok = mbar_wait_bounded(full, it & 1, err, 0x311);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        float *X = RX + p * kRowFloats;
+        float r[64];
+        gather(r, X, q, s_in, std::make_integer_sequence<int, 64>{});
+        __syncwarp();
+        to_matrix3(r);
+        factor4(r, c_fwd);
+        store_quadrant<true, false>(X, r4, c4, r);
+        __syncwarp();
+        quadrant_product(r, X, WM, r4, c4);
+        __syncwarp();
+        factor4(r, c_inv);
+        from_matrix3(r);
+        scatter(r, X, q, s_out, std::make_integer_sequence<int, 64>{});
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            for (int i = 0; i < nv; ++i) bulk_store(out + (r0 + i) * 256, RX + i * kRowFloats, 1024);
+            bulk_commit();
+        }
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+// Per CTA: sum over the CTA's rows of rho(x)^T rho(dy), written as a
+// row-major 16 x 16 partial at partial[blockIdx.x * 256] (the 8 product
+// slots of the warp are summed by shuffles at the end).
+__global__ void __launch_bounds__(32)
+    gp_layer_dw_kernel(const float *__restrict__ x, const float *__restrict__ dy,
+                       float *__restrict__ partial, int64_t batch, int64_t nbatches, int *err) {
+    extern __shared__ __align__(16) float sm[];
+    float *const RX = sm, *const RG = sm + kRegion;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + 2 * kRegion);
+    const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
+    const int r4 = q >> 1, c4 = r4 ^ (q & 1);
+    if (lane == 0) {
+        mbar_init(full, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    float s_in[4], s_out[4];
+    lane_signs(q, s_in, s_out);
+    const float c_fwd = r4 ? 1.0f : -1.0f;
+    float acc[64];
+#pragma unroll
+    for (int s = 0; s < 64; ++s) acc[s] = 0.0f;
+    bool ok = true;
+    int64_t bt = blockIdx.x;
+    for (int it = 0; bt < nbatches && ok; bt += gridDim.x, ++it) {
+        const int64_t r0 = bt * 8;
+        const int nv = (int)std::min<int64_t>(8, batch - r0);
+        if (lane == 0) {
+            bulk_wait_read<0>();
+            mbar_arrive_expect_tx(full, (uint32_t)nv * 2048u);
+            for (int i = 0; i < nv; ++i) {
+                bulk_load(RX + i * kRowFloats, x + (r0 + i) * 256, 1024, full);
+                bulk_load(RG + i * kRowFloats, dy + (r0 + i) * 256, 1024, full);
+            }
+        }
+        ok = mbar_wait_bounded(full, it & 1, err, 0x312);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        float *X = RX + p * kRowFloats, *G = RG + p * kRowFloats;
+        const bool valid = p < nv;  // slots past the end of the batch add nothing
+        float r[64];
+        gather(r, X, q, s_in, std::make_integer_sequence<int, 64>{});
+        __syncwarp();
+        to_matrix3(r);
+        factor4(r, c_fwd);
+        if (!valid) {
+#pragma unroll
+            for (int s = 0; s < 64; ++s) r[s] = 0.0f;
+        }
+        store_quadrant<true, true>(X, r4, c4, r);  // rho(x)^T as the A operand
+        gather(r, G, q, s_in, std::make_integer_sequence<int, 64>{});
+        __syncwarp();
+        to_matrix3(r);
+        factor4(r, c_fwd);
+        if (!valid) {  // stale shared memory may hold non-finite values: zero both operands
+#pragma unroll
+            for (int s = 0; s < 64; ++s) r[s] = 0.0f;
+        }
+        store_quadrant<false, false>(G, r4, c4, r);  // rho(dy) as the B operand
+        __syncwarp();
+        quadrant_product<false, true>(acc, X, G, r4, c4);
+        __syncwarp();
+    }
+#pragma unroll
+    for (int s = 0; s < 64; ++s)
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) acc[s] += __shfl_xor_sync(0xffffffffu, acc[s], o);
+    if (p == 0) {
+        // entry (i, j) of quadrant (r4, c4) is matrix entry (2i + r4, 2j + c4)
+        float *dst = partial + (size_t)blockIdx.x * 256;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[(2 * i + r4) * 16 + 2 * j + c4] = acc[slot_ij(i, j)];
+    }
+}
+
+// dW = sum of the partials (fp64), then dw = rho^-1(dW) by warp 0.
+__global__ void __launch_bounds__(256)
+    gp_layer_dw_finish_kernel(const float *__restrict__ partial, int nparts, float *__restrict__ dw) {
+    __shared__ float W[256];
+    {
+        const int e = threadIdx.x;
+        double s = 0.0;
+        for (int k = 0; k < nparts; ++k) s += (double)partial[(size_t)k * 256 + e];
+        W[e] = (float)s;
+    }
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x, q = lane & 3, r4 = q >> 1, c4 = r4 ^ (q & 1);
+    float s_in[4], s_out[4];
+    lane_signs(q, s_in, s_out);
+    float r[64];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[slot_ij(i, j)] = W[(2 * i + r4) * 16 + 2 * j + c4];
+    factor4(r, r4 ? -1.0f : 1.0f);
+    from_matrix3(r);
+    if (lane < 4) scatter(r, dw, q, s_out, std::make_integer_sequence<int, 64>{});
+}
+
+int occupancy_grid(const void *kern, int smem, int64_t nbatches, const DeviceInfo &di) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32, smem) != cudaSuccess ||
+        per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    return (int)std::max<int64_t>(1, std::min<int64_t>(nbatches, (int64_t)per_sm * di.sm_count));
+}
+
 template <int MODE>
 int launch_mat16(const float *x, const float *y, float *out, int64_t batch, cudaStream_t s) {
     DeviceInfo di;
@@ -443,6 +646,60 @@ int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, floa
     kern<<<grid, 32, kBwdSmem, s>>>(a, b, g, ga, gb, batch, nb, err);
     e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_mat16_bwd_kernel");
+}
+
+constexpr int kApplySmem = (kWFloats + kRegion) * 4 + 64;
+constexpr int kDwSmem = 2 * kRegion * 4 + 64;
+
+int gp_layer_apply(const float *wm, const float *in, float *out, int64_t batch, cudaStream_t s) {
+    if (batch == 0) return CB_OK;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    int *err = nullptr;
+    if ((st = device_error_word(&err))) return st;
+    static int grid_cap = 0;
+    if (grid_cap == 0) grid_cap = occupancy_grid((const void *)gp_layer_apply_kernel, kApplySmem, 1 << 30, di);
+    const int64_t nb = (batch + 7) / 8;
+    const int grid = (int)std::min<int64_t>(nb, grid_cap);
+    gp_layer_apply_kernel<<<grid, 32, kApplySmem, s>>>(in, out, wm, batch, nb, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_layer_apply_kernel");
+}
+
+int gp_layer_dw_parts(int64_t batch) {
+    DeviceInfo di;
+    if (device_info(&di)) return -1;
+    static int grid_cap = 0;
+    if (grid_cap == 0) grid_cap = occupancy_grid((const void *)gp_layer_dw_kernel, kDwSmem, 1 << 30, di);
+    const int64_t nb = std::max<int64_t>(1, (batch + 7) / 8);
+    return (int)std::min<int64_t>(nb, grid_cap);
+}
+
+int gp_layer_dw(const float *x, const float *dy, float *dw, float *partial, int64_t batch,
+                cudaStream_t s) {
+    int *err = nullptr;
+    int st = device_error_word(&err);
+    if (st) return st;
+    const int parts = gp_layer_dw_parts(batch);
+    if (parts <= 0) return cuda_fail(cudaGetLastError(), "gp layer dw sizing");
+    const int64_t nb = (batch + 7) / 8;
+    cudaError_t e = cudaSuccess;
+    if (batch > 0)
+        gp_layer_dw_kernel<<<parts, 32, kDwSmem, s>>>(x, dy, partial, batch, nb, err);
+    else
+        e = cudaMemsetAsync(partial, 0, (size_t)parts * 256 * sizeof(float), s);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch gp_layer_dw_kernel");
+    gp_layer_dw_finish_kernel<<<1, 256, 0, s>>>(partial, parts, dw);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_layer_dw_finish_kernel");
+}
+
+int gp_layer_weight(const float *w, float *mats, cudaStream_t s) {
+    gp_layer_weight_kernel<<<1, 32, 0, s>>>(w, mats);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_layer_weight_kernel");
 }
 
 }  // namespace cb

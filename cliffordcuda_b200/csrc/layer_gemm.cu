@@ -979,3 +979,53 @@ extern "C" int cb_layer_backward(int op, const float *mats, const float *x, cons
     e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch layer fold kernels");
 }
+
+// ----------------------------------------- GP layer of Cl(8,0), matrix route --
+namespace {
+int gp8_aligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+extern "C" int cb_layer_gp8_prepare(const float *w, float *mats, void *stream) {
+    if (!w || !mats || !gp8_aligned(mats)) {
+        set_error("layer_gp8_prepare: null or unaligned pointer");
+        return CB_ERR_INVALID;
+    }
+    return gp_layer_weight(w, mats, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cb_layer_gp8_forward(const float *mats, const float *x, float *y, int64_t batch,
+                                    void *stream) {
+    if (batch < 0 || (batch > 0 && (!mats || !x || !y || x == y))) {
+        set_error("layer_gp8_forward: invalid arguments");
+        return CB_ERR_INVALID;
+    }
+    if (batch > 0 && (!gp8_aligned(mats) || !gp8_aligned(x) || !gp8_aligned(y))) {
+        set_error("layer_gp8_forward: rows must be 16-byte aligned");
+        return CB_ERR_INVALID;
+    }
+    return gp_layer_apply(mats, x, y, batch, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cb_layer_gp8_backward(const float *mats, const float *x, const float *dy,
+                                     float *dx, float *dw, int64_t batch, void *workspace,
+                                     int64_t workspace_bytes, void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (batch < 0 || !mats || (batch > 0 && (!x || !dy)) || (dx && (dx == dy || dx == x))) {
+        set_error("layer_gp8_backward: invalid arguments");
+        return CB_ERR_INVALID;
+    }
+    if (batch > 0 && (!gp8_aligned(x) || !gp8_aligned(dy) || (dx && !gp8_aligned(dx)))) {
+        set_error("layer_gp8_backward: rows must be 16-byte aligned");
+        return CB_ERR_INVALID;
+    }
+    int st;
+    if (dx && (st = gp_layer_apply(mats + kGpLayerWFloats, dy, dx, batch, s))) return st;
+    if (!dw) return CB_OK;
+    const int parts = gp_layer_dw_parts(batch);
+    if (parts <= 0 || !workspace || workspace_bytes < (int64_t)parts * 256 * 4) {
+        set_error("layer_gp8_backward: workspace of %lld bytes needed",
+                  (long long)(parts > 0 ? parts : 0) * 256 * 4);
+        return CB_ERR_INVALID;
+    }
+    return gp_layer_dw(x, dy, dw, static_cast<float *>(workspace), batch, s);
+}

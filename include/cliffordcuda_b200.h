@@ -120,6 +120,26 @@ CB_API int cb_layer_backward(int op, const float *mats, const float *x, const fl
                              uint32_t zero_mask, void *workspace, int64_t workspace_bytes,
                              void *stream);
 
+/*
+ * GeometricProductLayer of Cl(8,0) (Euclidean metric, n = 8) through the real
+ * 16 x 16 matrix representation of the algebra: y = x w is rho(y) = rho(x) W
+ * with W = rho(w), one 16 x 16 product per row with a fixed matrix, instead
+ * of the 256 x 256 contraction; dx = rho^-1(rho(dy) W^T) and
+ * dw = rho^-1(sum over rows of rho(x)^T rho(dy)). Same results as the
+ * cb_layer_* route for this layer (to fp32 rounding). Replaces, for this
+ * layer, the same reference path as cb_layer_* (layers.py:43-47).
+ *   prepare:  w (256 floats) -> mats (the cb_layer_* buffer; 576 floats used)
+ *   forward:  y = x w, rows 16-byte aligned
+ *   backward: dx (skipped if NULL) and dw (skipped if NULL); workspace as
+ *             sized by cb_layer_workspace_bytes(8, batch, ...)
+ */
+CB_API int cb_layer_gp8_prepare(const float *w, float *mats, void *stream);
+CB_API int cb_layer_gp8_forward(const float *mats, const float *x, float *y, int64_t batch,
+                                void *stream);
+CB_API int cb_layer_gp8_backward(const float *mats, const float *x, const float *dy, float *dx,
+                                 float *dw, int64_t batch, void *workspace,
+                                 int64_t workspace_bytes, void *stream);
+
 /* ---------------------------------------------------------------- rotors --
  * A compiled rotor is two caller-owned device buffers:
  *   cs    (fp32, cs_floats entries): per grade k = 0..n the C(n,k) x C(n,k)

@@ -112,3 +112,32 @@ def test_layer_config3_shape_properties():
     assert rel_l2(layer.weight.grad.cpu().numpy().ravel(), dw_ref) <= 1e-5
     del wrep
     _lib.device_status(DEV)
+
+
+@pytest.mark.parametrize("batch", [5, 1037])
+def test_gp8_routes_agree(batch):
+    """The GeometricProductLayer of Cl(8,0) runs through the 16 x 16 matrix
+    representation (cb_layer_gp8_*); the dense tcgen05 route (cb_layer_*)
+    stays reachable. Both against the oracle and against each other."""
+    from cliffordcuda_b200 import layer_ops
+    n, metric = 8, (1,) * 8
+    rng = np.random.default_rng(batch)
+    x = rng.standard_normal((batch, 256)).astype(np.float32)
+    g = rng.standard_normal((batch, 256)).astype(np.float32)
+    w = (rng.standard_normal(256) / 16).astype(np.float32)
+    ref = oracle_layer("gp", n, metric, x, w, g)
+    outs = []
+    for dense in (False, True):
+        wt = torch.tensor(w, device=DEV).view(1, -1).requires_grad_(True)
+        xt = torch.tensor(x, device=DEV, requires_grad=True)
+        if dense:
+            y = layer_ops._LayerFn.apply(xt, wt, "gp", n, metric)
+        else:
+            y = layer_ops.layer_product("gp", xt, wt, n, metric)
+        y.backward(torch.tensor(g, device=DEV))
+        got = (y.detach().cpu().numpy(), xt.grad.cpu().numpy(), wt.grad.cpu().numpy().ravel())
+        for name, a, b in zip(("y", "dx", "dw"), got, ref):
+            assert rel_l2(a, b) <= REL_L2_TOL, f"dense={dense} {name}: {rel_l2(a, b):.3e}"
+        outs.append(got)
+    for a, b in zip(*outs):
+        assert rel_l2(a, b) < 1e-5
