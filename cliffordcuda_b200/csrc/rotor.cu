@@ -468,7 +468,7 @@ __global__ void rotor_reduce_kernel(const float *__restrict__ partial, int parts
 // keeps the number of squarings set by B alone, and the result is scaled back.
 __global__ void __launch_bounds__(1024)
     rotor_compile_bwd_kernel(const double *__restrict__ state, const float *__restrict__ dcs,
-                             int n, float *__restrict__ dbeta) {
+                             int n, float *__restrict__ dbeta, bool stage) {
     const Layout L = make_layout(n);
     const int nn = n * n, m = 2 * n;
     __shared__ double dRm[kMaxN * kMaxN];
@@ -478,6 +478,18 @@ __global__ void __launch_bounds__(1024)
     __shared__ double dscale;
     const double *Bm = state;
     const double *C64 = state + 2 * nn;
+    // n <= 8: the minors and dC staged in shared memory (dynamic, 12 B per entry)
+    extern __shared__ __align__(16) unsigned char stage_raw[];
+    if (stage) {
+        double *c64s = reinterpret_cast<double *>(stage_raw);
+        float *dcss = reinterpret_cast<float *>(c64s + L.total);
+        for (int e = threadIdx.x; e < L.total; e += blockDim.x) {
+            c64s[e] = C64[e];
+            dcss[e] = dcs[e];
+        }
+        C64 = c64s;
+        dcs = dcss;
+    }
     for (int bp = threadIdx.x; bp < L.D; bp += blockDim.x) rank[bp] = blade_rank(bp);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
@@ -497,7 +509,7 @@ __global__ void __launch_bounds__(1024)
                 if (__popc(j) != k1) continue;
                 const uint32_t Jp = (j & lowq) | ((j & ~lowq) << 1);
                 const uint32_t J = Jp | (1u << q);
-                const double t = (double)__ldg(&dcs[rowI + rank[J]]) * __ldg(&C64[rowIp + rank[Jp]]);
+                const double t = (double)dcs[rowI + rank[J]] * C64[rowIp + rank[Jp]];
                 acc += ((a + __popc(Jp & lowq)) & 1) ? -t : t;
             }
         }
@@ -716,7 +728,17 @@ extern "C" int cb_rotor_compile_bwd(const double *state, const float *dcs, int n
     }
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    rotor_compile_bwd_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(state, dcs, n, dbeta);
+    const Layout L = make_layout(n);
+    const size_t stage_bytes = (size_t)L.total * (sizeof(double) + sizeof(float));
+    const bool stage = stage_bytes <= (size_t)200 * 1024;
+    if (stage) {
+        cudaError_t e0 = cudaFuncSetAttribute(rotor_compile_bwd_kernel,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)stage_bytes);
+        if (e0 != cudaSuccess) return cuda_fail(e0, "cudaFuncSetAttribute(rotor_compile_bwd)");
+    }
+    rotor_compile_bwd_kernel<<<1, 1024, stage ? stage_bytes : 0, static_cast<cudaStream_t>(stream)>>>(
+        state, dcs, n, dbeta, stage);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch rotor_compile_bwd_kernel");
 }
