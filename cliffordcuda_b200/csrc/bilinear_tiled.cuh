@@ -200,11 +200,21 @@ __host__ __device__ inline size_t smem_bytes(int n, bool inner) {
 template <int MODE, int OPK>
 __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const float *yt,
                                       const float2 *tab, const float2 *tab2, int rowl, int kh,
-                                      int lgNH) {
+                                      int lgNH, bool skip_zero) {
     const int NH = 1 << lgNH;
 #pragma unroll 1
     for (int ih = 0; ih < NH; ++ih) {
         const int jh = ih ^ kh;
+        const float2 sg = tab[(ih << lgNH) | kh];
+        const float2 sg2 = OPK == OPK_INNER ? tab2[(ih << lgNH) | kh] : make_float2(0.0f, 0.0f);
+        // A step whose high-part factor is zero for the whole warp (a null
+        // generator in both high parts, or the product's predicate) adds
+        // nothing: skip its loads and FMAs. Enabled where such steps occur
+        // (skip_zero, warp-uniform): a warp then spans at most half the
+        // high-block outputs of a row, or a null generator sits in the high bits.
+        if (skip_zero &&
+            __all_sync(0xffffffffu, sg.x == 0.0f && sg.y == 0.0f && sg2.x == 0.0f && sg2.y == 0.0f))
+            continue;
         float xv[kBlk], yv[kBlk];
         load_block(xt, rowl + ih, xv);
         load_block(yt, rowl + jh, yv);
@@ -214,9 +224,7 @@ __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const
             for (int e = 0; e < kBlk; ++e)
                 if (popcl(e) & 1) xv[e] *= sx;
         }
-        const float2 sg = tab[(ih << lgNH) | kh];
         if (OPK == OPK_INNER) {
-            const float2 sg2 = tab2[(ih << lgNH) | kh];
             float y2[kBlk];
 #pragma unroll
             for (int e = 0; e < kBlk; ++e) y2[e] = yv[e];
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
                           const __grid_constant__ CUtensorMap my,
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
-                          uint32_t zero, int num_tiles, int *err) {
+                          uint32_t zero, int num_tiles, int *err, bool skip_zero) {
     extern __shared__ unsigned char smem_raw[];
     // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
@@ -297,14 +305,16 @@ __global__ void __launch_bounds__(kThreads, 3)
         const int tile = blockIdx.x + it * gridDim.x;
         if (tile >= num_tiles) break;
         const int s = it % kStages;
-        if (!mbar_wait_bounded(&full[s], (it / kStages) & 1, err, 0x101)) break;
+        // warp-uniform: the sweep below uses full-warp votes and shuffles
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / kStages) & 1, err, 0x101)))
+            break;
         float *xt = xs + s * kTileFloats;
         const float *yt = ys + s * kTileFloats;
 
         float acc[kBlk];
 #pragma unroll
         for (int e = 0; e < kBlk; ++e) acc[e] = 0.0f;
-        sweep<MODE, OPK>(acc, xt, yt, tab, tab2, rowl, kh, lgNH);
+        sweep<MODE, OPK>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
 
         if (MODE == CB_MODE_GRAD_A && parity(kh)) {
 #pragma unroll
@@ -399,7 +409,8 @@ int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int 
         return CB_ERR_UNSUPPORTED;
     }
     const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * di.sm_count);
-    kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err);
+    const bool skip_zero = n >= 9 || (zero >> kLow) != 0;
+    kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err, skip_zero);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "launch bilinear_tiled_kernel");
     return CB_OK;
