@@ -192,6 +192,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="row blocks the e2e step pipelines over copy-in / compute / copy-out")
     ap.add_argument("--no-blade-sum", action="store_true",
                     help="skip timing the blade-by-blade kernels beside the headline")
     ap.add_argument("--batch", type=int, default=None,
@@ -298,7 +300,8 @@ def main():
 
     e2e_value = None
     if not args.no_e2e:
-        e2e_value, host_out = run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier)
+        e2e_value, host_out = run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier,
+                                      chunks=args.e2e_chunks)
         # the pipelined host results equal the device-resident ones bit for bit
         for h, d in zip(host_out, (c, ga, gb)):
             if not torch.equal(h, d.cpu()):
@@ -338,8 +341,8 @@ def main():
                 "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 3 * B * D * 4,
                 "d2h_bytes_per_step": 3 * B * D * 4,
                 "path": "cliffordcuda_b200.geom_prod + autograd backward, pinned host "
-                        "buffers, copies inside the timed region, 8 row chunks pipelined "
-                        "over copy-in / compute / copy-out streams"},
+                        f"buffers, copies inside the timed region, {args.e2e_chunks} row "
+                        "chunks pipelined over copy-in / compute / copy-out streams"},
             "gpu_launches": 2 * K,
             "clocks": clk.summary(),
         }
