@@ -24,6 +24,13 @@ from . import products as _p
 GEMM_N = (7, 8)
 
 
+def _aligned(t):
+    """Contiguous with 16-byte aligned rows (the layer kernels stream rows with
+    TMA / bulk copies); offset views are copied."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _workspace(n, batch, device):
     wb = ctypes.c_int64()
     _lib.check(_lib.load().cb_layer_workspace_bytes(n, batch, ctypes.byref(wb)),
@@ -61,7 +68,7 @@ class _LayerFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x, mats = ctx.saved_tensors
-        dy = dy.contiguous()
+        dy = _aligned(dy)
         need_x, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         dx = torch.empty_like(x) if need_x else None
         dw = torch.empty(1 << ctx.n, device=x.device, dtype=torch.float32) if need_w else None
@@ -100,7 +107,7 @@ class _Gp8LayerFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x, mats = ctx.saved_tensors
-        dy = dy.contiguous()
+        dy = _aligned(dy)
         need_x, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         dx = torch.empty_like(x) if need_x else None
         dw = torch.empty(256, device=x.device, dtype=torch.float32) if need_w else None
@@ -114,15 +121,10 @@ class _Gp8LayerFn(torch.autograd.Function):
         return dx, (dw.view(ctx.wshape) if dw is not None else None)
 
 
-def _gp8_route(op, n, metric, x):
-    return (op == "gp" and n == 8 and all(m == 1 for m in metric)
-            and x.data_ptr() % 16 == 0)
-
-
 def layer_product(op, x, weight, n, metric):
-    if _gp8_route(op, n, metric, x.contiguous()):
-        return _Gp8LayerFn.apply(x.contiguous(), weight)
+    if op == "gp" and n == 8 and all(m == 1 for m in metric):
+        return _Gp8LayerFn.apply(_aligned(x), weight)
     if n in GEMM_N:
-        return _LayerFn.apply(x.contiguous(), weight, op, n, tuple(metric))
+        return _LayerFn.apply(_aligned(x), weight, op, n, tuple(metric))
     w = weight.expand_as(x).contiguous()
     return _p._product(op, x, w, metric)

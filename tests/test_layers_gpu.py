@@ -141,3 +141,30 @@ def test_gp8_routes_agree(batch):
         outs.append(got)
     for a, b in zip(*outs):
         assert rel_l2(a, b) < 1e-5
+
+
+@pytest.mark.parametrize("op,metric", [("gp", (1,) * 8), ("wedge", (1,) * 8),
+                                       ("lc", (1,) * 7 + (-1,))])
+def test_layer_unaligned_views(op, metric):
+    """x and the upstream gradient as views starting one float into their
+    buffers: the layer copies them to aligned rows and matches the oracle."""
+    n, batch = 8, 37
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((batch, 256)).astype(np.float32)
+    g = rng.standard_normal((batch, 256)).astype(np.float32)
+    w = (rng.standard_normal(256) / 16).astype(np.float32)
+    ref = oracle_layer(op, n, metric, x, w, g)
+    bx = torch.zeros(batch * 256 + 1, device=DEV)
+    bx[1:].copy_(torch.from_numpy(x).view(-1))
+    xt = bx[1:].view(batch, 256).requires_grad_(True)
+    bg = torch.zeros(batch * 256 + 1, device=DEV)
+    bg[1:].copy_(torch.from_numpy(g).view(-1))
+    cl = cc.CliffordAlgebra(list(metric), device=DEV)
+    layer = LAYERS[op](cl)
+    with torch.no_grad():
+        layer.weight.copy_(torch.tensor(w, device=DEV).view(1, -1))
+    y = layer(xt)
+    y.backward(bg[1:].view(batch, 256))
+    got = (y.detach().cpu().numpy(), xt.grad.cpu().numpy(), layer.weight.grad.cpu().numpy().ravel())
+    for name, a, b in zip(("y", "dx", "dw"), got, ref):
+        assert rel_l2(a, b) <= REL_L2_TOL, f"{op} {name}: {rel_l2(a, b):.3e}"
