@@ -60,11 +60,18 @@ def _apply_raw(cs, x, n, transpose=False):
     return y
 
 
+def _aligned(t):
+    """Contiguous with 16-byte aligned rows (the n = 7, 8 kernels read rows
+    through TMA); offset views are copied."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 class _ApplyFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, cs, x, n):
         cs = cs.contiguous()
-        x = x.contiguous()
+        x = _aligned(x)
         ctx.save_for_backward(cs, x)
         ctx.n = n
         return _apply_raw(cs, x, n)
@@ -73,7 +80,7 @@ class _ApplyFn(torch.autograd.Function):
     def backward(ctx, g):
         cs, x = ctx.saved_tensors
         n = ctx.n
-        g = g.contiguous()
+        g = _aligned(g)
         need_cs, need_x = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         dx = torch.empty_like(x) if need_x else None
         dcs = None

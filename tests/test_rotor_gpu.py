@@ -122,3 +122,28 @@ def test_config4_shape_properties():
     ny = torch.linalg.norm(y, dim=1)
     assert ((ny - nx).abs() / nx).max().item() < 1e-4
     _lib.device_status(DEV)
+
+
+def test_rotor_unaligned_views():
+    """x and the upstream gradient as views one float into their buffers:
+    apply_bivector copies them to aligned rows; results match the aligned run."""
+    n, batch = 8, 21
+    cl = algebra(n)
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    beta = (0.2 * torch.randn(1, 28, device=DEV, generator=gen)).requires_grad_(True)
+    x = torch.randn(batch, 256, device=DEV, generator=gen)
+    g = torch.randn(batch, 256, device=DEV, generator=gen)
+    bx = torch.zeros(batch * 256 + 1, device=DEV)
+    bx[1:].copy_(x.view(-1))
+    bg = torch.zeros(batch * 256 + 1, device=DEV)
+    bg[1:].copy_(g.view(-1))
+    xv = bx[1:].view(batch, 256).requires_grad_(True)
+    y = cl.apply_bivector(beta, xv)
+    y.backward(bg[1:].view(batch, 256))
+    x2 = x.clone().requires_grad_(True)
+    beta2 = beta.detach().clone().requires_grad_(True)
+    y2 = cl.apply_bivector(beta2, x2)
+    y2.backward(g)
+    assert rel_l2(y.detach().cpu().numpy(), y2.detach().cpu().numpy()) < 1e-6
+    assert rel_l2(xv.grad.cpu().numpy(), x2.grad.cpu().numpy()) < 1e-6
+    assert rel_l2(beta.grad.cpu().numpy(), beta2.grad.cpu().numpy()) < 1e-6
