@@ -466,6 +466,8 @@ __global__ void rotor_reduce_kernel(const float *__restrict__ partial, int parts
 // The adjoint Frechet derivative is linear in dRm, so dRm enters the block
 // exponential divided by a power of two near its largest entry (exact), which
 // keeps the number of squarings set by B alone, and the result is scaled back.
+constexpr int kSubsetsPerPopc = 128;  // >= C(9, k), the subsets of n - 1 <= 9 generators
+
 __global__ void __launch_bounds__(1024)
     rotor_compile_bwd_kernel(const double *__restrict__ state, const float *__restrict__ dcs,
                              int n, float *__restrict__ dbeta, bool stage) {
@@ -491,13 +493,23 @@ __global__ void __launch_bounds__(1024)
         dcs = dcss;
     }
     for (int bp = threadIdx.x; bp < L.D; bp += blockDim.x) rank[bp] = blade_rank(bp);
+    // the subsets of the other n - 1 generators grouped by size, in a fixed order
+    __shared__ unsigned short subsets[kMaxN * kSubsetsPerPopc];
+    __shared__ int nsubsets[kMaxN];
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < kMaxN; ++k) nsubsets[k] = 0;
+        for (uint32_t j = 0; j < (1u << (n - 1)); ++j) {
+            const int k = __popc(j);
+            subsets[k * kSubsetsPerPopc + nsubsets[k]++] = (unsigned short)j;
+        }
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const uint32_t sub = 1u << (n - 1);
     for (int e = warp; e < nn; e += nwarps) {
         const int p = e / n, q = e % n;
         const uint32_t lowp = (1u << p) - 1, lowq = (1u << q) - 1;
-        double acc = 0.0;
+        double acc = 0.0, acc2 = 0.0;
         for (uint32_t i = lane; i < sub; i += 32) {
             const uint32_t Ip = (i & lowp) | ((i & ~lowp) << 1);  // I' (skips generator p)
             const int k1 = __popc(i), k = k1 + 1;
@@ -505,14 +517,24 @@ __global__ void __launch_bounds__(1024)
             const int a = __popc(Ip & lowp);
             const uint32_t I = Ip | (1u << p);
             const int rowI = L.coff[k] + rank[I] * ck, rowIp = L.coff[k1] + rank[Ip] * ck1;
-            for (uint32_t j = 0; j < sub; ++j) {
-                if (__popc(j) != k1) continue;
+            const unsigned short *js = subsets + k1 * kSubsetsPerPopc;
+            const int nj = nsubsets[k1];
+            auto term = [&](uint32_t j) {
                 const uint32_t Jp = (j & lowq) | ((j & ~lowq) << 1);
                 const uint32_t J = Jp | (1u << q);
                 const double t = (double)dcs[rowI + rank[J]] * C64[rowIp + rank[Jp]];
-                acc += ((a + __popc(Jp & lowq)) & 1) ? -t : t;
+                return ((a + __popc(Jp & lowq)) & 1) ? -t : t;
+            };
+            // only the subsets J' of the same size; two independent chains of
+            // dependent shared-memory loads per step
+            int u = 0;
+            for (; u + 1 < nj; u += 2) {
+                acc += term(js[u]);
+                acc2 += term(js[u + 1]);
             }
+            if (u < nj) acc += term(js[u]);
         }
+        acc += acc2;
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) dRm[e] = acc;
     }
