@@ -39,9 +39,9 @@ FLOPS_PER_SUM = 2 * NNZ_GP            # one FMA per non-zero term
 BYTES_PER_SUM = 3 * D * 4             # two operand rows read, one row written
 BYTES_PER_BWD = 5 * D * 4             # a, b, g read; grad_a, grad_b written
 # DRAM bytes per row of one gp_mat16_bwd_kernel launch, from ncu: dram__bytes_read.sum
-# + dram__bytes_write.sum of a 262,144-row launch / rows (profiles/gp_mat16_cl8.md:
-# (805.4 + 496.8) MB / 262,144). Every row is read once and written once, so the
-# per-launch traffic is this times the batch.
+# + dram__bytes_write.sum of a 262,144-row launch / rows ((805.4 + 496.8) MB / 262,144).
+# Every row is read once and written once, so the per-launch traffic is this
+# times the batch.
 MEASURED_TRAFFIC_PER_BWD = (805.4e6 + 496.8e6) / 262144
 
 
@@ -298,10 +298,11 @@ def main():
     blade = blade_sum_path(a, b, g, c, ga, gb, metric, stream, dev, world, barrier,
                            fp32_peak) if not args.no_blade_sum else None
 
-    e2e_value = None
+    e2e_value, link = None, None
     if not args.no_e2e:
         e2e_value, host_out = run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier,
                                       chunks=args.e2e_chunks)
+        link = pinned_link_gbs(dev)
         # the pipelined host results equal the device-resident ones bit for bit
         for h, d in zip(host_out, (c, ga, gb)):
             if not torch.equal(h, d.cpu()):
@@ -331,10 +332,12 @@ def main():
                          "fwd": {"kernel": "gp_mat16_kernel", "ms_per_launch": fwd_ms,
                                  "gbs": BYTES_PER_SUM * B / (fwd_ms / 1000.0) / 1e9,
                                  "frac": BYTES_PER_SUM * B / (fwd_ms / 1000.0) / 1e9 / peak}},
-            "pct_fp32_peak": 100.0 * eff_tflops / fp32_peak,
-            "pct_fp32_peak_note": "effective: blade-by-blade flops (2 x 4^8 per product and "
-                                  "sum) over time against the nominal FP32 peak; the matrix "
-                                  "representation executes about 1/16 of those flops",
+            "blade_flop_equivalent_pct": 100.0 * eff_tflops / fp32_peak,
+            "blade_flop_equivalent_note": "not a roofline fraction: blade-by-blade flops "
+                                          "(2 x 4^8 per product and sum) the matrix route does "
+                                          "not execute, over time, against the nominal FP32 "
+                                          "peak; the FP32-peak fraction of the blade-by-blade "
+                                          "kernels is blade_sum_path.pct_fp32_peak",
             "blade_sum_path": blade,
             "cpu_baseline": cpu,
             "e2e": None if e2e_value is None else {
@@ -342,7 +345,11 @@ def main():
                 "d2h_bytes_per_step": 3 * B * D * 4,
                 "path": "cliffordcuda_b200.geom_prod + autograd backward, pinned host "
                         f"buffers, copies inside the timed region, {args.e2e_chunks} row "
-                        "chunks pipelined over copy-in / compute / copy-out streams"},
+                        "chunks pipelined over copy-in / compute / copy-out streams",
+                "pinned_link": link,
+                "link_bound_products_per_s": None if not link else
+                    world * min(link["h2d_gbs"], link["d2h_gbs"], link["bidir_gbs"] / 2) * 1e9
+                    / (3 * D * 4)},
             "gpu_launches": 2 * K,
             "clocks": clk.summary(),
         }
@@ -398,7 +405,9 @@ def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier, chunks=8):
     copies a, b, g in, runs cliffordcuda_b200.geom_prod + backward, and copies
     c, grad_a, grad_b out -- in `chunks` row blocks pipelined over three
     streams (copy-in, compute, copy-out) so the two PCIe directions and the
-    kernels overlap."""
+    kernels overlap, within a step and across steps: the copy-in of a chunk
+    waits only for the previous step's compute on that chunk's device rows,
+    and the copy-out of a step runs while the next step computes."""
     B = a.shape[0]
     ha, hb, hg = (t.cpu().pin_memory() for t in (a, b, g))
     hc, hga, hgb = (torch.empty_like(ha).pin_memory() for _ in range(3))
@@ -406,18 +415,20 @@ def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier, chunks=8):
     s_in = torch.cuda.Stream(dev)
     s_out = torch.cuda.Stream(dev)
     bounds = [(i * B // chunks, (i + 1) * B // chunks) for i in range(chunks)]
+    consumed = [None] * chunks      # compute of the chunk's device rows done
 
     def e2e_step():
         ev_in = []
-        for lo, hi in bounds:
+        for i, (lo, hi) in enumerate(bounds):
             with torch.cuda.stream(s_in):
-                s_in.wait_stream(stream)
+                if consumed[i] is not None:
+                    s_in.wait_event(consumed[i])
                 for d, h in ((da, ha), (db, hb), (dg, hg)):
                     d[lo:hi].copy_(h[lo:hi], non_blocking=True)
                 e = torch.cuda.Event()
                 e.record(s_in)
                 ev_in.append(e)
-        for (lo, hi), e in zip(bounds, ev_in):
+        for i, ((lo, hi), e) in enumerate(zip(bounds, ev_in)):
             stream.wait_event(e)
             xa = da[lo:hi].detach().requires_grad_(True)
             xb = db[lo:hi].detach().requires_grad_(True)
@@ -425,6 +436,7 @@ def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier, chunks=8):
             out.backward(dg[lo:hi])
             done = torch.cuda.Event()
             done.record(stream)
+            consumed[i] = done
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done)
                 hc[lo:hi].copy_(out.detach(), non_blocking=True)
@@ -432,17 +444,19 @@ def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier, chunks=8):
                 hgb[lo:hi].copy_(xb.grad, non_blocking=True)
                 for t in (out, xa.grad, xb.grad):
                     t.record_stream(s_out)
-        stream.wait_stream(s_out)
 
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize(dev)
     K2 = max(1, min(K, 5))
     barrier()
+    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    s_in.wait_stream(stream)       # the timed region starts before the first copy-in
     for _ in range(K2):
         e2e_step()
+    stream.wait_stream(s_out)      # ... and ends after the last copy-out
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
@@ -451,6 +465,42 @@ def run_e2e(cc, a, b, g, dev, stream, metric, K, world, barrier, chunks=8):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = t.item()
     return world * B * K2 / (e2e_ms / 1000.0), (hc, hga, hgb)
+
+
+def pinned_link_gbs(dev, nbytes=1 << 30, reps=3):
+    """Plain pinned-host <-> device copy bandwidth of this box, GB/s: H2D
+    alone, D2H alone, and both directions at once on two streams (the
+    ceiling the e2e step's copies run against)."""
+    n = nbytes // 4
+    h_src = torch.empty(n, dtype=torch.float32).pin_memory()
+    h_dst = torch.empty(n, dtype=torch.float32).pin_memory()
+    d_a = torch.empty(n, dtype=torch.float32, device=dev)
+    d_b = torch.empty(n, dtype=torch.float32, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(fn):
+        best = None
+        for _ in range(reps):
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize(dev)
+            dt = time.perf_counter() - t0
+            best = dt if best is None else min(best, dt)
+        return best
+
+    h2d = nbytes / timed(lambda: d_a.copy_(h_src, non_blocking=True)) / 1e9
+    d2h = nbytes / timed(lambda: h_dst.copy_(d_b, non_blocking=True)) / 1e9
+
+    def both():
+        with torch.cuda.stream(s1):
+            d_a.copy_(h_src, non_blocking=True)
+        with torch.cuda.stream(s2):
+            h_dst.copy_(d_b, non_blocking=True)
+    bidir = 2 * nbytes / timed(both) / 1e9
+    return {"h2d_gbs": round(h2d, 2), "d2h_gbs": round(d2h, 2), "bidir_gbs": round(bidir, 2),
+            "bytes": nbytes, "how": "one 1 GiB pinned copy, best of 3, host clock around "
+                                    "device syncs"}
 
 
 if __name__ == "__main__":

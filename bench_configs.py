@@ -39,9 +39,10 @@ HBM_GBS = float(PEAKS.get("hbm_gbs", 6650.0))
 BF16_TFLOPS = float(PEAKS.get("bf16_tflops", 1590.0))
 SM_MAX_MHZ = float(PEAKS.get("sm_max_mhz", 1965.0))
 # Nominal tcgen05 kind::tf32 rate at the maximum SM clock: one 128x256x8 MMA
-# per 128 cycles per SM = 4096 FLOP/clk/SM (cliffordcuda_b200/csrc/
-# probe_mma_rate.cu measures this per-clock rate). Higher, i.e. stricter, than
-# measured bf16 / 2, which carries cuBLAS's efficiency and the power cap.
+# per 128 cycles per SM = 4096 FLOP/clk/SM (the issue rate a stand-alone MMA
+# loop measured on a B200, for single CTAs and CTA pairs alike). Higher, i.e.
+# stricter, than measured bf16 / 2, which carries cuBLAS's efficiency and the
+# power cap.
 TF32_TFLOPS = 148 * 4096 * SM_MAX_MHZ * 1e6 / 1e12
 X3TF32_TFLOPS = TF32_TFLOPS / 3     # three tf32 MMAs per fp32-accurate product
 
@@ -192,7 +193,7 @@ def layer(args, world, rank, dev, T):
                     "rows_per_s": t["rows_per_s"], "useful_tflops": t["useful_tflops"],
                     "peak": X3TF32_TFLOPS, "frac": t["frac_3xtf32_peak"],
                     "peak_source": "nominal tf32 tensor rate at max SM clock (148 SMs x 4096 "
-                                   "FLOP/clk, per-clock rate measured by probe_mma_rate) / 3 "
+                                   "FLOP/clk, the measured per-clock MMA rate) / 3 "
                                    "(3xTF32 MMAs per product)",
                     "frac_of_measured_bf16_over_6": t["useful_tflops"] / (BF16_TFLOPS / 6)}
     return _line(args, world, "Cl(8,0) GeometricProductLayer training rows/s",

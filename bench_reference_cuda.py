@@ -9,6 +9,7 @@ a row subset (relative L2). One JSON line per workload. This is a
 measurement aid beside bench.py, not part of the product.
 
     python bench_reference_cuda.py [--workload headline|products|layer|rotor|pga|all]
+                                   [--out FILE]
 """
 from __future__ import annotations
 
@@ -81,6 +82,7 @@ def main():
     ap.add_argument("--workload", default="all")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--out", default=None, help="also append each JSON line to this file")
     args = ap.parse_args()
     ref = _ref()
     import cliffordcuda_b200 as ours
@@ -163,6 +165,9 @@ def main():
                         "rel_l2_dbivector_vs_this_library": rel(olay.bivector.grad,
                                                                lay.bivector.grad)})
         print(json.dumps(out), flush=True)
+        if args.out:
+            with open(args.out, "a") as f:
+                f.write(json.dumps(out) + "\n")
 
 
 if __name__ == "__main__":

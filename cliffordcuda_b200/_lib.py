@@ -21,6 +21,7 @@ STATUS_NAMES = {1: "CB_ERR_INVALID", 2: "CB_ERR_CUDA", 3: "CB_ERR_UNSUPPORTED",
                 4: "CB_ERR_DEVICE"}
 OPS = {"gp": 0, "wedge": 1, "inner": 2, "lc": 3, "rc": 4, "reg": 5}
 MODES = {"fwd": 0, "grad_a": 1, "grad_b": 2}
+MAPS = {"reverse": 0, "involute": 1, "conjugate": 2, "grade": 3, "dual": 4, "dual_t": 5}
 
 # Every symbol include/cliffordcuda_b200.h declares, with its ctypes signature.
 _i64, _i32, _u32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p
@@ -44,6 +45,9 @@ SIGNATURES = {
     "cb_rotor_apply_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _i64, _vp]),
     "cb_rotor_compile_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp]),
     "cb_rotor_apply_bwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
+    "cb_blade_map": (_i32, [_i32, _vp, _vp, _i64, _i32, _u32, _u32, _i32, _vp]),
+    "cb_norm_sq": (_i32, [_vp, _vp, _i64, _i32, _u32, _u32, _vp]),
+    "cb_norm_sq_bwd": (_i32, [_vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp]),
     "cb_last_error": (ctypes.c_char_p, []),
     "cb_device_status": (_i32, [_vp]),
     "cb_selftest_bounded_wait": (_i32, [_u32, _vp]),

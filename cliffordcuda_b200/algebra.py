@@ -11,6 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import _validate
+from . import blade_maps as _maps
 from . import products as _p
 
 
@@ -61,51 +62,36 @@ class CliffordAlgebra:
         self._check2(a, b)
         return _p.regressive_prod(a, b, metric=self.metric)
 
-    # ── sign-vector elementwise ops (algebra.py:195-336) ─────────────
-    # One-pass multiplies by a per-blade sign or weight vector; they run as
-    # torch elementwise ops on the device (not part of the kernel library).
-    def _grades(self):
-        if not hasattr(self, "_grade_vec"):
-            idx = torch.arange(self.dim, device=self.device)
-            k = torch.zeros(self.dim, device=self.device, dtype=torch.long)
-            for t in range(self.n):
-                k += (idx >> t) & 1
-            self._grade_vec = k
-        return self._grade_vec
-
+    # ── per-blade maps and the norm (algebra.py:195-336) ─────────────
+    # One pass each on the native kernels (cb_blade_map, cb_norm_sq), with
+    # autograd; `compile` is accepted for API compatibility and has no effect
+    # (the kernel already makes a single memory pass).
     def reverse(self, x):
         """Reversion: grade k -> (-1)^(k(k-1)/2)."""
         _validate._check_mv(x, "x", self.dim, self.device, self.dtype)
-        k = self._grades()
-        return x * torch.where(((k * (k - 1) // 2) % 2) == 1, -1.0, 1.0).to(self.dtype)
+        return _maps.blade_map("reverse", x, self.metric)
 
     def grade_involution(self, x):
+        """Grade involution: grade k -> (-1)^k."""
         _validate._check_mv(x, "x", self.dim, self.device, self.dtype)
-        k = self._grades()
-        return x * torch.where((k % 2) == 1, -1.0, 1.0).to(self.dtype)
+        return _maps.blade_map("involute", x, self.metric)
 
     def clifford_conjugation(self, x):
+        """Clifford conjugation: grade k -> (-1)^(k(k+1)/2)."""
         _validate._check_mv(x, "x", self.dim, self.device, self.dtype)
-        k = self._grades()
-        return x * torch.where(((k * (k + 1) // 2) % 2) == 1, -1.0, 1.0).to(self.dtype)
+        return _maps.blade_map("conjugate", x, self.metric)
 
     def grade_projection(self, x, grade):
+        """Keep the grade-`grade` coefficients, zero the others (same shape)."""
         if not 0 <= grade <= self.n:
             raise ValueError(f"grade must be in [0, {self.n}] for n={self.n}; got {grade}")
         _validate._check_mv(x, "x", self.dim, self.device, self.dtype)
-        return x * (self._grades() == grade).to(self.dtype)
-
-    def _metric_weights(self):
-        idx = torch.arange(self.dim, device=self.device)
-        w = torch.ones(self.dim, device=self.device)
-        for t in range(self.n):
-            w = w * torch.where(((idx >> t) & 1).bool(), float(self.metric[t]), 1.0)
-        return w.to(self.dtype)
+        return _maps.blade_map("grade", x, self.metric, grade)
 
     def norm_sq(self, x, compile=False):
         """<x x~>_0 = sum_b x_b^2 prod_{i in b} metric[i]; shape (batch,)."""
         _validate._check_mv(x, "x", self.dim, self.device, self.dtype)
-        return (x * x * self._metric_weights()).sum(-1)
+        return _maps.norm_sq(x, self.metric)
 
     def dual(self, x, compile=False):
         """x I^-1: a signed reversal of the coefficients (non-degenerate only)."""
@@ -114,18 +100,7 @@ class CliffordAlgebra:
                 "dual is undefined for degenerate metrics (any 0 in the "
                 "metric makes the pseudoscalar I non-invertible).")
         _validate._check_mv(x, "x", self.dim, self.device, self.dtype)
-        n, full = self.n, self.dim - 1
-        i_sq = (-1) ** (n * (n - 1) // 2)
-        for m in self.metric:
-            i_sq *= m
-        idx = torch.arange(self.dim, device=self.device)
-        a = full ^ idx
-        swaps = torch.zeros(self.dim, device=self.device, dtype=torch.long)
-        for t in range(n):
-            swaps += t * ((a >> t) & 1)
-        signs = float(i_sq) * torch.where((swaps % 2) == 1, -1.0, 1.0) * \
-            self._metric_weights().index_select(0, a)
-        return x.flip(-1) * signs.to(self.dtype)
+        return _maps.blade_map("dual", x, self.metric)
 
     # ── rotors (algebra.py:337-373) ──────────────────────────────────
     def _check_rotor_supported(self):

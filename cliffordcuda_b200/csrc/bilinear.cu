@@ -213,14 +213,24 @@ extern "C" int cb_bilinear_bwd(int op, const float *a, const float *b, const flo
                                uint32_t neg_mask, uint32_t zero_mask, void *stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int st = CB_OK;
-    if (grad_a && grad_b && grad_a != grad_b && cb::use_mat16(op, n, neg_mask, zero_mask, a, b, g) &&
+    // grad_a is written before the grad_b sum reads a, so no output may alias
+    // any of a, b, g or the other output, whatever kernel serves the call.
+    if (batch > 0) {
+        const void *outs[2] = {grad_a, grad_b};
+        for (const void *o : outs)
+            if (o && (o == a || o == b || o == g)) {
+                cb::set_error("gradient outputs must not alias an input");
+                return CB_ERR_INVALID;
+            }
+        if (grad_a && grad_a == grad_b) {
+            cb::set_error("grad_a and grad_b must be different buffers");
+            return CB_ERR_INVALID;
+        }
+    }
+    if (grad_a && grad_b && cb::use_mat16(op, n, neg_mask, zero_mask, a, b, g) &&
         cb::use_mat16(op, n, neg_mask, zero_mask, grad_a, grad_b, g)) {
         st = cb::check_args(op, CB_MODE_GRAD_A, b, g, grad_a, batch, n, neg_mask, zero_mask);
         if (!st) st = cb::check_args(op, CB_MODE_GRAD_B, a, g, grad_b, batch, n, neg_mask, zero_mask);
-        if (!st && (grad_a == a || grad_b == b)) {
-            cb::set_error("gradient outputs must not alias an input");
-            st = CB_ERR_INVALID;
-        }
         return st ? st : cb::gp_mat16_bwd(a, b, g, grad_a, grad_b, batch, s);
     }
     if (grad_a)

@@ -782,12 +782,13 @@ static __device__ __align__(256) float g_rotor_bwd_scratch[kNoAllocScratchFloats
 
 constexpr int kMaxScratchDevices = 64;
 static float *g_scratch_addr[kMaxScratchDevices];
-static cudaError_t g_scratch_err[kMaxScratchDevices];
-static std::once_flag g_scratch_once[kMaxScratchDevices];
+static std::mutex g_scratch_mutex;
 
 // Device address of the scratch array on the current device. In host code
-// the array's name is only a host-side stand-in, so the address is fetched
-// once per device, with that device current, and cached.
+// the array's name is only a host-side stand-in, so the address is looked up
+// with that device current and cached once the lookup succeeds; a failed
+// lookup (for example one attempted during stream capture) is reported and
+// tried again on the next call.
 int noalloc_scratch(float **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -796,13 +797,14 @@ int noalloc_scratch(float **out) {
         set_error("device ordinal %d out of range", dev);
         return CB_ERR_UNSUPPORTED;
     }
-    std::call_once(g_scratch_once[dev], [dev] {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
         void *p = nullptr;
-        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_rotor_bwd_scratch);
-        g_scratch_addr[dev] = (g_scratch_err[dev] == cudaSuccess) ? static_cast<float *>(p) : nullptr;
-    });
-    if (!g_scratch_addr[dev])
-        return cuda_fail(g_scratch_err[dev], "cudaGetSymbolAddress(rotor backward scratch)");
+        e = cudaGetSymbolAddress(&p, g_rotor_bwd_scratch);
+        if (e != cudaSuccess || !p)
+            return cuda_fail(e, "cudaGetSymbolAddress(rotor backward scratch)");
+        g_scratch_addr[dev] = static_cast<float *>(p);
+    }
     *out = g_scratch_addr[dev];
     return CB_OK;
 }

@@ -92,6 +92,41 @@ CB_API int cb_bilinear_bwd(int op, const float *a, const float *b, const float *
                            float *grad_a, float *grad_b, int64_t batch, int n,
                            uint32_t neg_mask, uint32_t zero_mask, void *stream);
 
+/* -------------------------------------------------------- blade maps --
+ * One-pass per-blade maps of CliffordAlgebra on (batch, 2^n) rows, 1 <= n <= 24.
+ * The factor of each blade comes from popcounts of its index; no tables.
+ * The reference computed these as torch elementwise multiplies by cached
+ * sign vectors (src/cliffordcuda/algebra.py:195-336); it had no kernel. */
+#define CB_MAP_REVERSE 0   /* (-1)^(k(k-1)/2), k = grade        algebra.py:195-206 */
+#define CB_MAP_INVOLUTE 1  /* (-1)^k                            algebra.py:278-286 */
+#define CB_MAP_CONJUGATE 2 /* (-1)^(k(k+1)/2)                   algebra.py:288-296 */
+#define CB_MAP_GRADE 3     /* keep grade `grade`, zero the rest algebra.py:298-307 */
+#define CB_MAP_DUAL 4      /* x I^-1: out[m] = s(~m) x[~m]      algebra.py:208-266 */
+#define CB_MAP_DUAL_T 5    /* transpose of the dual: out[m] = s(m) x[~m] (its backward) */
+
+/*
+ * out = map(x). `grade` is read only by CB_MAP_GRADE. The dual maps need a
+ * non-degenerate metric (zero_mask = 0) and out != x; the other maps may run
+ * in place (out == x). Replaces reverse / grade_involution /
+ * clifford_conjugation / grade_projection / dual of
+ * src/cliffordcuda/algebra.py:195-307 and the free function reverse of
+ * extensions/ga/inverse.py:64-67.
+ */
+CB_API int cb_blade_map(int kind, const float *x, float *out, int64_t batch, int n,
+                        uint32_t neg_mask, uint32_t zero_mask, int grade, void *stream);
+
+/*
+ * out[row] = sum_b x[row, b]^2 w_b, w_b = prod over the generators t of b of
+ * metric[t] (+1, -1 or 0): the squared norm <x x~>_0 of every row, fp32.
+ * Replaces CliffordAlgebra.norm_sq (src/cliffordcuda/algebra.py:309-336).
+ */
+CB_API int cb_norm_sq(const float *x, float *out, int64_t batch, int n, uint32_t neg_mask,
+                      uint32_t zero_mask, void *stream);
+
+/* Gradient of cb_norm_sq for upstream g (batch floats): dx = 2 w x g[row]. */
+CB_API int cb_norm_sq_bwd(const float *x, const float *g, float *dx, int64_t batch, int n,
+                          uint32_t neg_mask, uint32_t zero_mask, void *stream);
+
 /* ---------------------------------------------------------------- layers --
  * Shared-weight product layers y = op(x, w), w (1, 2^n) shared by the batch
  * (reference layers.py:30-76). Because op is bilinear, y = x M(w); the

@@ -104,6 +104,52 @@ void orc_product(int op, int mode, int n, const int *metric, int64_t batch,
     free(T);
 }
 
+/*
+ * As orc_product for the outputs k in [k0, k1) only, with the sign evaluated
+ * per term instead of from a (D, D) table, so that large n (the table is
+ * 4^n bytes) and parallel splits over k stay cheap. The sign is the same
+ * sigma as orc_sign: the reorder parity counts, for every generator a of i,
+ * the generators of j below a (a popcount of j masked below a); the metric
+ * multiplies over i & j.
+ */
+static int orc_sign_popc(uint32_t i, uint32_t j, uint32_t neg, uint32_t zero)
+{
+    uint32_t c = i & j;
+    if (c & zero) return 0;
+    int parity = __builtin_popcount(c & neg);
+    for (uint32_t rest = i; rest; rest &= rest - 1) {
+        int a = __builtin_ctz(rest);
+        parity += __builtin_popcount(j & ((1u << a) - 1u));
+    }
+    return (parity & 1) ? -1 : 1;
+}
+
+void orc_product_range(int op, int mode, int n, const int *metric, int64_t batch,
+                       const double *x, const double *y, double *out,
+                       uint32_t k0, uint32_t k1)
+{
+    uint32_t D = 1u << n, neg = 0, zero = 0;
+    for (int t = 0; t < n; ++t) {
+        if (metric[t] == -1) neg |= 1u << t;
+        if (metric[t] == 0) zero |= 1u << t;
+    }
+    for (int64_t r = 0; r < batch; ++r) {
+        const double *xr = x + r * D, *yr = y + r * D;
+        double *o = out + r * D;
+        for (uint32_t k = k0; k < k1; ++k) {
+            double acc = 0.0;
+            for (uint32_t i = 0; i < D; ++i) {
+                uint32_t P = (mode == ORC_GRAD_A) ? k : i;
+                uint32_t Q = (mode == ORC_FWD) ? (i ^ k) : (mode == ORC_GRAD_A ? i : k);
+                if (!orc_mask(op, P, Q)) continue;
+                int s = orc_sign_popc(P, Q, neg, zero);
+                if (s) acc += (double)s * xr[i] * yr[i ^ k];
+            }
+            o[k] = acc;
+        }
+    }
+}
+
 /* dual(x)[k] = x[~k] * sigma(~k, full) / I^2  (non-degenerate metrics only). */
 void orc_dual_signs(int n, const int *metric, double *ds)
 {

@@ -58,6 +58,9 @@ def lib():
                                      ctypes.POINTER(ctypes.c_int8)]
         L.orc_product.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ip,
                                   ctypes.c_int64, dp, dp, dp]
+        L.orc_product_range.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ip,
+                                        ctypes.c_int64, dp, dp, dp, ctypes.c_uint32,
+                                        ctypes.c_uint32]
         L.orc_regressive_fwd.argtypes = [ctypes.c_int, ip, ctypes.c_int64, dp, dp, dp]
         L.orc_regressive_bwd.argtypes = [ctypes.c_int, ip, ctypes.c_int64,
                                          dp, dp, dp, dp, dp]
@@ -117,6 +120,20 @@ def product(op, mode, n, metric, x, y, threads=None):
     out = np.empty_like(x)
     m = _metric_arr(metric)
     L = lib()
+
+    if n >= 11:
+        # no (D, D) table; the output blades are split over the threads
+        nt = threads or os.cpu_count() or 1
+        step = (D + nt - 1) // nt
+
+        def run_k(k0):
+            L.orc_product_range(OPS[op], MODES[mode], n, m, x.shape[0], _dptr(x), _dptr(y),
+                                _dptr(out), k0, min(D, k0 + step))
+
+        if x.shape[0]:
+            with ThreadPoolExecutor(nt) as ex:
+                list(ex.map(run_k, range(0, D, step)))
+        return out
 
     def run(rng):
         s, e = rng
@@ -234,13 +251,12 @@ def givens_chain_apply(n, Rm, x):
     return y
 
 
-def rotor_grads_torch(n, beta, x, g):
-    """fp64 autograd truth for the rotor: (y, dL/dx, dL/dbeta) with
-    L = <g, y>, y = x C(Rm), Rm = torch.linalg.matrix_exp(2 (M - M^T))."""
+def _rotor_C_torch(n, beta_t):
+    """C(beta) in torch fp64, differentiable: C[I, J] = det Rm[I, J] on
+    equal-grade blade pairs, Rm = matrix_exp(2 (M - M^T)), M[p, q] = beta_pq
+    for p < q in lex-pair order (reference algebra.py:127, eigh_exp.cu:270-322)."""
     import torch
     D = 1 << n
-    beta_t = torch.tensor(np.asarray(beta, dtype=np.float64).reshape(-1), requires_grad=True)
-    x_t = torch.tensor(np.asarray(x, dtype=np.float64).reshape(-1, D), requires_grad=True)
     iu = torch.triu_indices(n, n, offset=1)
     M = torch.zeros(n, n, dtype=torch.float64).index_put((iu[0], iu[1]), beta_t)
     Rm = torch.linalg.matrix_exp(2.0 * (M - M.T))
@@ -257,11 +273,46 @@ def rotor_grads_torch(n, beta, x, g):
                 ci = [t for t in range(n) if (J >> t) & 1]
                 col.append(torch.linalg.det(Rm[ri][:, ci]))
         cols.append(torch.stack(col))
-    C = torch.stack(cols, dim=1)  # C[I, J]
+    return torch.stack(cols, dim=1)  # C[I, J]
+
+
+def rotor_grads_torch(n, beta, x, g):
+    """fp64 autograd truth for the rotor: (y, dL/dx, dL/dbeta) with
+    L = <g, y>, y = x C(Rm), Rm = torch.linalg.matrix_exp(2 (M - M^T))."""
+    import torch
+    D = 1 << n
+    beta_t = torch.tensor(np.asarray(beta, dtype=np.float64).reshape(-1), requires_grad=True)
+    x_t = torch.tensor(np.asarray(x, dtype=np.float64).reshape(-1, D), requires_grad=True)
+    C = _rotor_C_torch(n, beta_t)
     y = x_t @ C
     g_t = torch.tensor(np.asarray(g, dtype=np.float64).reshape(-1, D))
     (y * g_t).sum().backward()
     return y.detach().numpy(), x_t.grad.numpy(), beta_t.grad.numpy()
+
+
+def rotor_dbeta_from_G(n, beta, G):
+    """dL/dbeta for L = <g, x C(beta)> summed over a batch, given only
+    G = sum over rows of x^T g (D x D, fp64): L = sum_IJ C[I, J] G[I, J], so
+    the batch enters through G alone and large batches cost one GEMM."""
+    import torch
+    beta_t = torch.tensor(np.asarray(beta, dtype=np.float64).reshape(-1), requires_grad=True)
+    C = _rotor_C_torch(n, beta_t)
+    (C * torch.as_tensor(np.asarray(G, dtype=np.float64))).sum().backward()
+    return beta_t.grad.numpy()
+
+
+def layer_dw_from_G(op, n, metric, G):
+    """Weight gradient of a product layer y = op(x, w) summed over the batch,
+    from G = sum over rows of x^T dy (D x D, fp64): the reference's
+    expand_as formulation (layers.py:43-47) sums grad_b(x, dy) over rows, and
+    grad_b[k] = sum_i s(i, k) x[i] dy[i ^ k], so dw[k] = sum_i s(i, k) G[i, i ^ k].
+    Products gp, wedge, inner, lc, rc (not the regressive one)."""
+    D = 1 << n
+    S = sign_table(n, metric, op).astype(np.float64)   # S[P, Q] with (P, Q) = (i, k)
+    i = np.arange(D).reshape(-1, 1)
+    k = np.arange(D).reshape(1, -1)
+    G = np.asarray(G, dtype=np.float64)
+    return (S * G[i, i ^ k]).sum(axis=0)
 
 
 # ---------------------------------------------------- torch einsum port --
@@ -301,3 +352,55 @@ class EinsumProduct:
             d = lambda x: x.index_select(-1, self.comp) * self.ds
             return d(self._wedge_like(d(A), d(B)))
         return self._wedge_like(A, B)
+
+
+# ------------------------------------------------------------ blade maps --
+
+def _grades(n):
+    return np.array([bin(i).count("1") for i in range(1 << n)])
+
+
+def blade_map(kind, n, metric, x, grade=None):
+    """Per-blade maps of CliffordAlgebra in float64 (reference
+    src/cliffordcuda/algebra.py): reverse (:195-206, (-1)^(k(k-1)/2)),
+    involute (:278-286, (-1)^k), conjugate (:288-296, (-1)^(k(k+1)/2)),
+    grade (:298-307, keep grade `grade`), dual (:208-266: out[m] = s(a) x[a],
+    a = ~m, s(a) = (1/I^2) (-1)^(sum of a's generator positions) prod_{t in a}
+    metric[t]) and dual_t, the dual's transpose (out[m] = s(m) x[~m])."""
+    D = 1 << n
+    x = np.asarray(x, dtype=np.float64).reshape(-1, D)
+    k = _grades(n)
+    if kind == "reverse":
+        return x * np.where((k * (k - 1) // 2) % 2 == 1, -1.0, 1.0)
+    if kind == "involute":
+        return x * np.where(k % 2 == 1, -1.0, 1.0)
+    if kind == "conjugate":
+        return x * np.where((k * (k + 1) // 2) % 2 == 1, -1.0, 1.0)
+    if kind == "grade":
+        return x * (k == grade)
+    if kind in ("dual", "dual_t"):
+        if 0 in metric:
+            raise ValueError("dual needs a non-degenerate metric")
+        i_sq = (-1) ** (n * (n - 1) // 2) * int(np.prod(metric))
+        idx = np.arange(D)
+        a = (D - 1) ^ idx if kind == "dual" else idx
+        pos = np.zeros(D, dtype=np.int64)
+        mprod = np.ones(D)
+        for t in range(n):
+            bit = (a >> t) & 1
+            pos += t * bit
+            mprod *= np.where(bit == 1, float(metric[t]), 1.0)
+        s = i_sq * np.where(pos % 2 == 1, -1.0, 1.0) * mprod
+        return x[:, (D - 1) ^ idx] * s
+    raise ValueError(kind)
+
+
+def norm_sq(n, metric, x):
+    """sum_b x_b^2 prod_{t in b} metric[t], float64 (algebra.py:309-336)."""
+    D = 1 << n
+    x = np.asarray(x, dtype=np.float64).reshape(-1, D)
+    w = np.ones(D)
+    idx = np.arange(D)
+    for t in range(n):
+        w *= np.where((idx >> t) & 1 == 1, float(metric[t]), 1.0)
+    return (x * x * w).sum(-1)

@@ -84,36 +84,6 @@ def test_layer_ragged_batches(batch):
         assert rel_l2(a, b) <= REL_L2_TOL
 
 
-def test_layer_config3_shape_properties():
-    """Config 3 per-GPU shape: x (524,288 x 256), w ~ N(0, 1/256), dY ~ N(0,1).
-    Sampled rows of y and dx against the oracle; dw against the batch-by-batch
-    kernel's grad_b summed over the batch (expand_as formulation)."""
-    from cliffordcuda_b200.products import bilinear_raw
-    batch, n, metric = 524_288, 8, (1,) * 8
-    gen = torch.Generator(device=DEV).manual_seed(3)
-    x = torch.randn(batch, 256, device=DEV, generator=gen)
-    dy = torch.randn(batch, 256, device=DEV, generator=gen)
-    cl = cc.CliffordAlgebra(list(metric), device=DEV)
-    layer = cc.GeometricProductLayer(cl)
-    with torch.no_grad():
-        layer.weight.copy_(torch.randn(1, 256, device=DEV, generator=gen) / 16)
-    xr = x.clone().requires_grad_(True)
-    y = layer(xr)
-    y.backward(dy)
-    rows = torch.randperm(batch, generator=torch.Generator().manual_seed(2))[:64].to(DEV)
-    w = layer.weight.detach().cpu().numpy().ravel()
-    ref_y, ref_dx, _ = oracle_layer("gp", n, metric, x[rows].cpu().numpy(), w,
-                                    dy[rows].cpu().numpy())
-    assert rel_l2(y[rows].detach().cpu().numpy(), ref_y) <= REL_L2_TOL
-    assert rel_l2(xr.grad[rows].cpu().numpy(), ref_dx) <= REL_L2_TOL
-    wrep = layer.weight.detach().expand(batch, 256).contiguous()
-    dw_rows = bilinear_raw("gp", "grad_b", x, dy, n, metric)
-    dw_ref = dw_rows.double().sum(0).cpu().numpy()
-    assert rel_l2(layer.weight.grad.cpu().numpy().ravel(), dw_ref) <= 1e-5
-    del wrep
-    _lib.device_status(DEV)
-
-
 @pytest.mark.parametrize("batch", [5, 1037])
 def test_gp8_routes_agree(batch):
     """The GeometricProductLayer of Cl(8,0) runs through the 16 x 16 matrix

@@ -136,6 +136,8 @@ def test_tiled_matches_generic():
     ("gp", 7, (1,) * 6 + (-1,), 1 << 20),           # config 2
     ("wedge", 7, (1,) * 6 + (-1,), 1 << 20),
     ("inner", 7, (1,) * 6 + (-1,), 1 << 20),
+    ("lc", 7, (1,) * 6 + (-1,), 1 << 20),
+    ("rc", 7, (1,) * 6 + (-1,), 1 << 20),
     ("gp", 10, (1,) * 9 + (0,), 131072),            # config 5
     ("lc", 10, (1,) * 9 + (0,), 131072),
 ])

@@ -53,7 +53,8 @@ def _both(n, batch, seed):
     return (dx.cpu().numpy(), dcs.cpu().numpy()), (dx_ref.cpu().numpy(), dcs_ref.cpu().numpy())
 
 
-@pytest.mark.parametrize("n,batches", [(8, (300_000, 1_000)), (7, (5_000, 200_000))])
+@pytest.mark.parametrize("n,batches", [(8, (300_000, 1_000)), (7, (5_000, 200_000)),
+                                       (8, (2_097_152, 3))])
 def test_noalloc_matches_workspace_entry_point_twice(n, batches):
     for call, batch in enumerate(batches):
         (dx, dcs), (dx_ref, dcs_ref) = _both(n, batch, seed=10 * n + call)
