@@ -238,7 +238,7 @@ int gemm3x_kmajor(int D, const float *A, const float *Bhi, const float *Blo, flo
 int gemm3x_mn_parts(int64_t rows);
 int gemm3x_mn(int D, const float *X, const float *dY, float *partial, int64_t rows, int parts,
               cudaStream_t s);
-int reduce_partials(const float *partial, int parts, int DD, float *G, cudaStream_t s);
+int reduce_partials(const float *partial, int parts, int D, float *G, cudaStream_t s);  // G is D x D
 int split_mats(const float *M, float *mats, int D, cudaStream_t s);
 
 // Cl(8,0) geometric product through the 16 x 16 real matrix representation

@@ -29,7 +29,9 @@
 // warps 2-3 split each landed A tile (both tiles in the MN kernel) into tf32
 // hi and lo parts in place, warps 4-7 drain TMEM (tcgen05.ld); the K-major
 // kernel stages 32x32 chunks of Y in 128B-swizzled shared buffers and
-// TMA-stores them.
+// TMA-stores them. The CTA-pair MN kernel has six converter warps (2-7) and
+// its epilogue in warps 8-11. The MN kernels restart their TMEM accumulation
+// every 256 rows and add the segments into their partial in fp32.
 //
 // 3xTF32: every operand v is split as hi = v with the low 13 mantissa bits
 // cleared (exactly representable in tf32) and lo = v - hi (exact in fp32);
@@ -396,8 +398,58 @@ struct MNSmem {
     static constexpr int STAGE = 4 * OP_BYTES;      // X hi, X lo, dY hi, dY lo
     static constexpr int BYTES = 1024 + MN_NSTAGE * STAGE + 256;
     static constexpr int HALVES = D / BM;           // M = D split into 128-row MMAs
-    static constexpr int TMEM_COLS = (HALVES * D < 32) ? 32 : HALVES * D;
+    static constexpr int ACC_COLS = HALVES * D;     // one D x D accumulator
+    static constexpr int NACC = (2 * ACC_COLS <= 512) ? 2 : 1;
+    static constexpr int TMEM_COLS = (NACC * ACC_COLS < 32) ? 32 : NACC * ACC_COLS;
 };
+
+// Rows of K accumulated in one TMEM accumulator before the epilogue adds it
+// into the CTA's partial in global memory. The tensor core rounds its fp32
+// accumulator at every MMA (three per 8 rows with 3xTF32), so a long K range
+// in one accumulator loses accuracy with the square root of its length or
+// faster; short segments summed in fp32 by the epilogue, then across CTAs in
+// double, keep G at fp32 accuracy for millions of rows. Two accumulators
+// alternate so the epilogue of one segment overlaps the MMAs of the next.
+constexpr int kSegChunks = 16;  // 16 chunks of BKR = 16 rows: 256 rows per segment
+
+// Storage order of a D x D partial of G: for each block of 128 rows, column
+// groups of four, then the 128 rows, then the four columns:
+//     off(row, col) = (row / 128) * 128 * D + ((col / 4) * 128 + row % 128) * 4 + col % 4
+// so that the 32 lanes of an epilogue warp (32 consecutive rows, the TMEM
+// lanes) touch 512 contiguous bytes with each float4 access.
+__host__ __device__ __forceinline__ size_t partial_off(int D, int row, int col) {
+    return (size_t)(row >> 7) * 128 * D + ((size_t)(col >> 2) * 128 + (row & 127)) * 4 + (col & 3);
+}
+
+// Epilogue of one segment for the 32 TMEM lanes of this warp: add columns
+// [0, D) of accumulator row `row` (TMEM address taddr) into the partial, or
+// store them for the first segment.
+__device__ __forceinline__ void drain_segment(uint32_t taddr, float *part, int D, int row,
+                                              bool first) {
+    float4 *base = reinterpret_cast<float4 *>(part + partial_off(D, row, 0));
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(taddr + c * 32, v);
+        float4 *dst = base + (size_t)c * 8 * 128;  // column group 8c, this row
+        float4 old[8];
+        if (!first) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) old[u] = dst[u * 128];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            float4 a = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            if (!first) {
+                a.x += old[u].x;
+                a.y += old[u].y;
+                a.z += old[u].z;
+                a.w += old[u].w;
+            }
+            dst[u * 128] = a;
+        }
+    }
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -413,8 +465,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char *stage0 = base;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + MN_NSTAGE * MN_STAGE);
     uint64_t *full = bars, *conv = bars + MN_NSTAGE, *empty = bars + 2 * MN_NSTAGE,
-             *accfull = bars + 3 * MN_NSTAGE;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * MN_NSTAGE + 1);
+             *accfull = bars + 3 * MN_NSTAGE, *accempty = bars + 3 * MN_NSTAGE + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * MN_NSTAGE + 4);
     auto op = [&](int s, int which) { return stage0 + s * MN_STAGE + which * MN_OP_BYTES; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -427,7 +479,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&conv[s], 64);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accfull, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&accfull[a], 1);
+            mbar_init(&accempty[a], 4);  // the four epilogue warps
+        }
         fence_barrier_init();
         prefetch_tensormap(&mX);
         prefetch_tensormap(&mG);
@@ -457,7 +512,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = idesc_tf32(BM, D, true, true);
         for (int c = 0; c < nchunks && ok; ++c) {
             const int s = c % MN_NSTAGE;
-            if (lane == 0) ok = mbar_wait_bounded(&conv[s], (c / MN_NSTAGE) & 1, err, 0x212);
+            const int seg = c / kSegChunks, a = seg % S::NACC;
+            const bool seg_first = (c % kSegChunks) == 0;
+            const bool seg_last = (c % kSegChunks) == kSegChunks - 1 || c == nchunks - 1;
+            // accumulator a is free once the epilogue drained its previous segment
+            if (lane == 0 && seg_first && seg >= S::NACC)
+                ok = mbar_wait_bounded(&accempty[a], (seg / S::NACC - 1) & 1, err, 0x215);
+            if (lane == 0 && ok) ok = mbar_wait_bounded(&conv[s], (c / MN_NSTAGE) & 1, err, 0x212);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
@@ -474,14 +535,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t moff = h * 4 * MN_BOX_BYTES + koff;
                         const uint64_t dxh = mnmajor_desc(xh + moff, MN_BOX_BYTES);
                         const uint64_t dxl = mnmajor_desc(xl + moff, MN_BOX_BYTES);
-                        const uint32_t dcol = tmem + h * D;
-                        mma_tf32(dcol, dxh, dgh, idesc, (c | kk) ? 1u : 0u);
+                        const uint32_t dcol = tmem + a * S::ACC_COLS + h * D;
+                        mma_tf32(dcol, dxh, dgh, idesc, (seg_first && kk == 0) ? 0u : 1u);
                         mma_tf32(dcol, dxh, dgl, idesc, 1u);
                         mma_tf32(dcol, dxl, dgh, idesc, 1u);
                     }
                 }
                 mma_commit(&empty[s]);
-                if (c == nchunks - 1) mma_commit(accfull);
+                if (seg_last) mma_commit(&accfull[a]);
             }
             __syncwarp();
         }
@@ -500,25 +561,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int q = warp & 3;
         float *dst0 = partial + (size_t)blockIdx.x * D * D;
-        if (nchunks > 0 && (ok = mbar_wait_bounded(accfull, 0, err, 0x214))) {
+        const int nseg = (nchunks + kSegChunks - 1) / kSegChunks;
+        for (int seg = 0; seg < nseg && ok; ++seg) {
+            const int a = seg % S::NACC;
+            if (!(ok = mbar_wait_bounded(&accfull[a], (seg / S::NACC) & 1, err, 0x214))) break;
             tc_fence_after();
             for (int h = 0; h < S::HALVES; ++h) {
                 const int i = h * 128 + q * 32 + lane;
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + h * D;
-#pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(taddr + c * 32, v);
-                    float4 *dst = reinterpret_cast<float4 *>(dst0 + (size_t)i * D + c * 32);
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-                }
+                const uint32_t taddr =
+                    tmem + ((uint32_t)(q * 32) << 16) + a * S::ACC_COLS + h * D;
+                drain_segment(taddr, dst0, D, i, seg == 0);
             }
-        } else if (nchunks == 0) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accempty[a]);
+        }
+        if (nchunks == 0) {
             for (int h = 0; h < S::HALVES; ++h) {
                 const int i = h * 128 + q * 32 + lane;
-                for (int k = 0; k < D; ++k) dst0[(size_t)i * D + k] = 0.0f;
+                for (int k = 0; k < D; ++k) dst0[partial_off(D, i, k)] = 0.0f;
             }
         }
     }
@@ -555,13 +616,16 @@ __global__ void split_mats_kernel(const float *M, float *mats, int D) {
     mats[3 * DD + e] = lo;
 }
 
-// G[e] = sum over partials, accumulated in double in a fixed order.
-__global__ void reduce_partials_kernel(const float *partial, int parts, int DD, float *G) {
+// G[row][col] = sum over partials (stored in partial_off order), accumulated
+// in double in a fixed order.
+__global__ void reduce_partials_kernel(const float *partial, int parts, int D, float *G) {
     const int e = blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= DD) return;
+    if (e >= D * D) return;
     double s = 0.0;
-    for (int p = 0; p < parts; ++p) s += (double)partial[(size_t)p * DD + e];
-    G[e] = (float)s;
+    for (int p = 0; p < parts; ++p) s += (double)partial[(size_t)p * D * D + e];
+    const int h = e / (128 * D), rem = e % (128 * D);
+    const int row = h * 128 + (rem & 511) / 4, col = (rem / 512) * 4 + (rem & 3);
+    G[row * D + col] = (float)s;
 }
 
 __global__ void column_sum_kernel(const float *A, int D, float *out) {
@@ -607,9 +671,14 @@ struct MNPairSmem {
     static constexpr int STAGE = 4 * OP_BYTES;          // X raw, X lo, dY raw, dY lo
     static constexpr int NSTAGE = 6;
     static constexpr int BYTES = 1024 + NSTAGE * STAGE + 256;
-    static constexpr int TMEM_COLS = 256;
+    static constexpr int ACC_COLS = 256;                // one 128 x 256 accumulator per CTA
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;      // two, alternating per segment
     static constexpr int CONV_WARPS = 6;                // warps 2-7
 };
+// Warps of gemm_mn_pair_kernel: 0 TMA, 1 TMEM allocation + MMA issue (even
+// CTA), 2-7 converters, 8-11 epilogue. The epilogue drains one segment while
+// the converters and the MMA work on the next, so it needs warps of its own.
+constexpr int kPairMNThreads = 384;
 
 // lo = v - (v with the low 13 mantissa bits cleared), v read from `raw`.
 __device__ __forceinline__ void split_lo(const float4 *raw, float4 *lo, int count, int t, int nt) {
@@ -622,7 +691,7 @@ __device__ __forceinline__ void split_lo(const float4 *raw, float4 *lo, int coun
     }
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairMNThreads, 1)
     gemm_mn_pair_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mG,
                         float *__restrict__ partial, int64_t rows, int64_t rows_per_part, int *err) {
     using S = MNPairSmem;
@@ -634,8 +703,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     unsigned char *const base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     unsigned char *stage0 = base;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stage0 + NS * S::STAGE);
-    uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * NS + 1);
+    uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS, *accfull = bars + 3 * NS,
+             *accempty = bars + 3 * NS + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * NS + 4);
     auto op = [&](int s, int which) { return stage0 + s * S::STAGE + which * S::OP_BYTES; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -651,7 +721,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(&conv[s], 2 * S::CONV_WARPS);  // converter warps of both CTAs
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accfull, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&accfull[a], 1);
+            mbar_init(&accempty[a], 8);  // the epilogue warps of both CTAs (even CTA's counts)
+        }
         fence_barrier_init();
         prefetch_tensormap(&mX);
         prefetch_tensormap(&mG);
@@ -686,7 +759,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = idesc_tf32(2 * BM, D, true, true);
             for (int c = 0; c < nchunks && ok; ++c) {
                 const int s = c % NS;
-                if (lane == 0)
+                const int seg = c / kSegChunks, a = seg & 1;
+                const bool seg_first = (c % kSegChunks) == 0;
+                const bool seg_last = (c % kSegChunks) == kSegChunks - 1 || c == nchunks - 1;
+                // accumulator a is free once both CTAs drained its previous segment
+                if (lane == 0 && seg_first && seg >= 2)
+                    ok = mbar_wait_bounded(&accempty[a], (seg / 2 - 1) & 1, err, 0x225,
+                                           2000000000ull, true);
+                if (lane == 0 && ok)
                     ok = mbar_wait_bounded(&conv[s], (c / NS) & 1, err, 0x222, 2000000000ull, true);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
@@ -701,17 +781,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const uint64_t dxl = mnmajor_desc(xl + koff, MN_BOX_BYTES);
                         const uint64_t dgh = mnmajor_desc(gh + koff, MN_BOX_BYTES);
                         const uint64_t dgl = mnmajor_desc(gl + koff, MN_BOX_BYTES);
-                        mma_tf32_pair(tmem, dxh, dgh, idesc, (c | kk) ? 1u : 0u);
-                        mma_tf32_pair(tmem, dxh, dgl, idesc, 1u);
-                        mma_tf32_pair(tmem, dxl, dgh, idesc, 1u);
+                        const uint32_t acc = tmem + a * S::ACC_COLS;
+                        mma_tf32_pair(acc, dxh, dgh, idesc, (seg_first && kk == 0) ? 0u : 1u);
+                        mma_tf32_pair(acc, dxh, dgl, idesc, 1u);
+                        mma_tf32_pair(acc, dxl, dgh, idesc, 1u);
                     }
                     mma_commit_pair(&empty[s]);
-                    if (c == nchunks - 1) mma_commit_pair(accfull);
+                    if (seg_last) mma_commit_pair(&accfull[a]);
                 }
                 __syncwarp();
             }
         }
-    } else {
+    } else if (warp < 2 + S::CONV_WARPS) {
         const int t = threadIdx.x - 64;
         for (int c = 0; c < nchunks && ok; ++c) {
             const int s = c % NS;
@@ -724,24 +805,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(&conv[s], 0);
         }
-        if (warp >= 4) {  // epilogue: TMEM lane quarter warp % 4
+    } else {
+        {  // epilogue warps 8-11: TMEM lane quarter warp % 4
             const int q = warp & 3;
             const int i = (int)rank * S::HALF + q * 32 + lane;
-            float *dst0 = partial + (size_t)part * D * D + (size_t)i * D;
-            if (nchunks > 0 && ok && (ok = mbar_wait_bounded(accfull, 0, err, 0x224))) {
+            float *dst0 = partial + (size_t)part * D * D;
+            const int nseg = (nchunks + kSegChunks - 1) / kSegChunks;
+            for (int seg = 0; seg < nseg && ok; ++seg) {
+                const int a = seg & 1;
+                if (!(ok = mbar_wait_bounded(&accfull[a], (seg / 2) & 1, err, 0x224))) break;
                 tc_fence_after();
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-#pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(taddr + c * 32, v);
-                    float4 *dst = reinterpret_cast<float4 *>(dst0 + c * 32);
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-                }
-            } else if (nchunks == 0) {
-                for (int k = 0; k < D; ++k) dst0[k] = 0.0f;
+                drain_segment(tmem + ((uint32_t)(q * 32) << 16) + a * S::ACC_COLS, dst0, D, i,
+                              seg == 0);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(&accempty[a], 0);
+            }
+            if (nchunks == 0) {
+                for (int k = 0; k < D; ++k) dst0[partial_off(D, i, k)] = 0.0f;
             }
         }
     }
@@ -752,9 +833,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 
-// Split of the batch for G = X^T dY: about 512 rows per partial keeps the
-// fp32 accumulation in TMEM short (the partials are summed in double), at
-// most 8 partials per SM.
+// Split of the batch for G = X^T dY: about 512 rows per partial, at most 8
+// partials per SM (the partials are summed in double; within a partial the
+// TMEM accumulation restarts every kSegChunks chunks).
 constexpr int kRowsPerPart = 512;
 int mn_parts(const DeviceInfo &di, int64_t batch) {
     const int64_t want = (batch + kRowsPerPart - 1) / kRowsPerPart;
@@ -831,7 +912,7 @@ int launch_mn(const float *x, const float *dy, float *partial, int64_t batch, in
         e = cudaFuncSetAttribute(gemm_mn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  MNPairSmem::BYTES);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_mn_pair)");
-        gemm_mn_pair_kernel<<<2 * parts, kThreads, MNPairSmem::BYTES, s>>>(mX, mG, partial, batch,
+        gemm_mn_pair_kernel<<<2 * parts, kPairMNThreads, MNPairSmem::BYTES, s>>>(mX, mG, partial, batch,
                                                                              rows_per_part, err);
     } else {
         auto kern = gemm_mn_kernel<D>;
@@ -867,8 +948,8 @@ int gemm3x_mn(int D, const float *X, const float *dY, float *partial, int64_t ro
     return CB_ERR_UNSUPPORTED;
 }
 
-int reduce_partials(const float *partial, int parts, int DD, float *G, cudaStream_t s) {
-    reduce_partials_kernel<<<(DD + 255) / 256, 256, 0, s>>>(partial, parts, DD, G);
+int reduce_partials(const float *partial, int parts, int D, float *G, cudaStream_t s) {
+    reduce_partials_kernel<<<(D * D + 255) / 256, 256, 0, s>>>(partial, parts, D, G);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch reduce_partials_kernel");
 }
@@ -968,7 +1049,7 @@ extern "C" int cb_layer_backward(int op, const float *mats, const float *x, cons
         st = n == 8 ? launch_mn<256>(x, dy, partial, batch, parts, s)
                     : launch_mn<128>(x, dy, partial, batch, parts, s);
         if (st) return st;
-        reduce_partials_kernel<<<blocks, 256, 0, s>>>(partial, parts, (int)DD, G);
+        reduce_partials_kernel<<<blocks, 256, 0, s>>>(partial, parts, D, G);
     } else {
         e = cudaMemsetAsync(G, 0, DD * 4, s);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(G)");

@@ -722,7 +722,7 @@ extern "C" int cb_rotor_apply_bwd(const float *cs, const float *x, const float *
         float *partial = static_cast<float *>(workspace);
         float *G = partial + (size_t)parts * DD;
         if ((st = gemm3x_mn(L.D, x, g, partial, batch, parts, s))) return st;
-        if ((st = reduce_partials(partial, parts, (int)DD, G, s))) return st;
+        if ((st = reduce_partials(partial, parts, L.D, G, s))) return st;
         rotor_gather_dc_kernel<<<(L.total + 255) / 256, 256, 0, s>>>(G, n, dcs);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(e, "launch rotor_gather_dc_kernel");
