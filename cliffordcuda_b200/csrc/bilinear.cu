@@ -11,6 +11,9 @@ namespace cb {
 template <int MODE>
 int bilinear_tiled(int op, const float *x, const float *y, float *out, int64_t batch, int n,
                    uint32_t neg, uint32_t zero, cudaStream_t stream);
+template <int MODE>
+int bilinear_wide(int op, const float *x, const float *y, float *out, int64_t batch, int n,
+                  uint32_t neg, uint32_t zero, cudaStream_t stream);
 
 namespace {
 
@@ -18,8 +21,9 @@ constexpr int kThreads = 256;
 
 // One block stages rows of x and y in shared memory and evaluates every term
 // with the sign computed from popcounts. Used for metrics whose low five
-// generators do not all square to +1, for n < 5 or n > 10, for pointers that
-// are not 16-byte aligned, and for the regressive product, evaluated as
+// generators do not all square to +1, for n < 5, for pointers that are not
+// 16-byte aligned, and for the regressive product (n <= 12; larger rows take
+// bilinear_generic_global_kernel), evaluated as
 // dual o wedge o dual (reference _shared/_einsum_refs.py:86-124) with the
 // dual's signed reversal applied while staging and storing:
 //   fwd:    X' = D a, Y' = D b,   out = D t
@@ -92,6 +96,55 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// As bilinear_generic_kernel for rows too large to stage (2^n > 4096): one
+// thread per output coefficient, operands read through the caches (the
+// lanes of a warp share x[i] and read 32 neighbouring y[i ^ k]).
+template <int MODE>
+__global__ void __launch_bounds__(kThreads)
+    bilinear_generic_global_kernel(int op, const float *__restrict__ x,
+                                   const float *__restrict__ y, float *__restrict__ out,
+                                   int64_t batch, int n, uint32_t neg, uint32_t zero) {
+    const uint32_t D = 1u << n, full = D - 1;
+    const bool reg = (op == CB_OP_REG);
+    const int base_op = reg ? CB_OP_WEDGE : op;
+    const float inv_isq = reg ? (float)blade_sign(full, full, neg, zero) : 1.0f;
+    auto dual_sign = [&](uint32_t i) -> float {
+        return (float)blade_sign(full ^ i, full, neg, zero) * inv_isq;
+    };
+    const int64_t total = batch << n;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = e >> n;
+        const uint32_t k = (uint32_t)(e & full);
+        const float *xr = x + row * D;
+        const float *yr = y + row * D;
+        float acc = 0.0f;
+        for (uint32_t i = 0; i < D; ++i) {
+            const uint32_t j = i ^ k;
+            const uint32_t P = (MODE == CB_MODE_GRAD_A) ? k : i;
+            const uint32_t Q = (MODE == CB_MODE_FWD) ? j : (MODE == CB_MODE_GRAD_A ? i : k);
+            if (!op_mask(base_op, P, Q)) continue;
+            const int s = blade_sign(P, Q, neg, zero);
+            if (s == 0) continue;
+            float xv, yv;
+            if (!reg) {
+                xv = xr[i];
+                yv = yr[j];
+            } else {
+                xv = dual_sign(i) * xr[i ^ full];
+                yv = (MODE == CB_MODE_FWD ? dual_sign(j) : dual_sign(j ^ full)) * yr[j ^ full];
+            }
+            acc = fmaf(s > 0 ? xv : -xv, yv, acc);
+        }
+        if (!reg)
+            out[row * D + k] = acc;
+        else if (MODE == CB_MODE_FWD)
+            out[row * D + (k ^ full)] = dual_sign(k ^ full) * acc;
+        else
+            out[row * D + (k ^ full)] = dual_sign(k) * acc;
+    }
+}
+
 template <int MODE>
 int launch_generic(int op, const float *x, const float *y, float *out, int64_t batch, int n,
                    uint32_t neg, uint32_t zero, cudaStream_t stream) {
@@ -99,6 +152,15 @@ int launch_generic(int op, const float *x, const float *y, float *out, int64_t b
     int st = device_info(&di);
     if (st) return st;
     const int D = 1 << n;
+    if (n > 12) {
+        const int64_t total = batch << n;
+        const int grid =
+            (int)std::min<int64_t>((total + kThreads - 1) / kThreads, (int64_t)di.sm_count * 8);
+        bilinear_generic_global_kernel<MODE>
+            <<<grid, kThreads, 0, stream>>>(op, x, y, out, batch, n, neg, zero);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch bilinear_generic_global_kernel");
+    }
     const int rpb = D >= kThreads ? 1 : kThreads / D;
     const size_t smem = (size_t)2 * rpb * D * sizeof(float);
     auto kern = bilinear_generic_kernel<MODE>;
@@ -126,6 +188,19 @@ bool use_tiled(int op, int n, uint32_t neg, uint32_t zero, const void *x, const 
     return true;
 }
 
+// The large-n kernel (bilinear_wide.cuh): same sign requirements as the
+// tiled one, 11 <= n <= 16.
+bool use_wide(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
+              const void *o, int64_t batch) {
+    if (op == CB_OP_REG) return false;
+    if (n < 11 || n > 16) return false;
+    if ((neg | zero) & 31u) return false;
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!al(x) || !al(y) || !al(o)) return false;
+    if ((uint64_t)batch * (1u << n) / 32 >= (1ull << 31)) return false;
+    return true;
+}
+
 int check_args(int op, int mode, const void *x, const void *y, const void *out, int64_t batch,
                int n, uint32_t neg, uint32_t zero) {
     if (op < CB_OP_GP || op > CB_OP_REG) {
@@ -136,8 +211,8 @@ int check_args(int op, int mode, const void *x, const void *y, const void *out, 
         set_error("mode %d out of range", mode);
         return CB_ERR_INVALID;
     }
-    if (n < 1 || n > 12) {
-        set_error("n = %d outside 1..12", n);
+    if (n < 1 || n > 16) {
+        set_error("n = %d outside 1..16", n);
         return CB_ERR_UNSUPPORTED;
     }
     if (batch < 0) {
@@ -180,6 +255,16 @@ int bilinear(int op, int mode, const float *x, const float *y, float *out, int64
             return bilinear_tiled<CB_MODE_GRAD_A>(op, x, y, out, batch, n, neg, zero, stream);
         default:
             return bilinear_tiled<CB_MODE_GRAD_B>(op, x, y, out, batch, n, neg, zero, stream);
+        }
+    }
+    if (use_wide(op, n, neg, zero, x, y, out, batch)) {
+        switch (mode) {
+        case CB_MODE_FWD:
+            return bilinear_wide<CB_MODE_FWD>(op, x, y, out, batch, n, neg, zero, stream);
+        case CB_MODE_GRAD_A:
+            return bilinear_wide<CB_MODE_GRAD_A>(op, x, y, out, batch, n, neg, zero, stream);
+        default:
+            return bilinear_wide<CB_MODE_GRAD_B>(op, x, y, out, batch, n, neg, zero, stream);
         }
     }
     switch (mode) {

@@ -39,7 +39,7 @@ def test_version():
 @pytest.mark.parametrize("args,code", [
     ((9, 0, 8, 1), 1),        # op out of range
     ((0, 7, 8, 1), 1),        # mode out of range
-    ((0, 0, 13, 1), 3),       # n too large
+    ((0, 0, 17, 1), 3),       # n too large
     ((0, 0, 0, 1), 3),        # n too small
     ((0, 0, 8, -1), 1),       # negative batch
     ((0, 0, 8, 4), 1),        # null pointers
