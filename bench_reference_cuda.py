@@ -20,10 +20,65 @@ import sys
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 REF = os.path.join(ROOT, "baseline", "_ref")
-os.environ.setdefault("XDG_CACHE_HOME", os.path.join(ROOT, "baseline", "_ref_build"))
-os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+BUILD = os.path.join(ROOT, "baseline", "_ref_build")
 sys.dont_write_bytecode = True
 
+
+def prepare_reference_env():
+    """Point the reference's torch JIT at baseline/_ref_build for sm_100. When
+    its extensions were built there already (they travel with the tree), mark
+    the build outputs newer than their sources so that ninja reuses them
+    instead of rebuilding them (a copied tree need not keep modification
+    times in order)."""
+    os.environ["XDG_CACHE_HOME"] = BUILD
+    os.environ["TORCH_EXTENSIONS_DIR"] = os.path.join(BUILD, "cliffordcuda", "torch_extensions")
+    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    ext = os.environ["TORCH_EXTENSIONS_DIR"]
+    if os.path.isdir(ext):
+        import time
+        now = time.time()
+        for d, _, files in os.walk(ext):
+            for f in files:
+                if f == "lock":
+                    os.remove(os.path.join(d, f))
+                else:
+                    os.utime(os.path.join(d, f), (now, now))
+
+
+# The reference's own extension loaders (each wraps torch.utils.cpp_extension.load).
+_LOADERS = [
+    ("cliffordcuda.extensions.ga.geom_prod", "load_geom_prod_cuda"),
+    ("cliffordcuda.extensions.ga.geom_prod_tiled", "load_geom_prod_tiled_cuda"),
+    ("cliffordcuda.extensions.ga.wedge_prod.chunk", "load_wedge_prod_cuda"),
+    ("cliffordcuda.extensions.ga.inner_prod.chunk", "load_inner_prod_cuda"),
+    ("cliffordcuda.extensions.ga.left_contract", "load_contract_cuda"),
+    ("cliffordcuda.extensions.rotor.eigh_exp", "load_eigh_exp_cuda"),
+    ("cliffordcuda.extensions.rotor.givens_factor", "load_givens_factor_cuda"),
+    ("cliffordcuda.extensions.rotor.givens_apply.mb_perm_packed",
+     "load_givens_apply_mb_perm_packed_cuda"),
+]
+
+
+def build_reference_extensions():
+    """JIT-build (or load) all of the reference's extensions at once, one
+    thread per extension: the reference builds each on first use, one after
+    the other, which takes about ten minutes on a fresh tree."""
+    import importlib
+    from concurrent.futures import ThreadPoolExecutor
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+
+    def one(spec):
+        mod, fn = spec
+        getattr(importlib.import_module(mod), fn)()
+
+    mods = [importlib.import_module(m) for m, _ in _LOADERS]  # imports stay serial
+    del mods
+    with ThreadPoolExecutor(len(_LOADERS)) as ex:
+        list(ex.map(one, _LOADERS))
+
+
+prepare_reference_env()
 import torch  # noqa: E402
 
 
@@ -33,6 +88,7 @@ def _ref():
                                      "unavailable": "baseline/_ref not installed"}))
     sys.path.insert(0, REF)
     import cliffordcuda
+    build_reference_extensions()
     return cliffordcuda
 
 

@@ -2,7 +2,8 @@
 
 The unmodified reference is installed under baseline/_ref (pip --target, no
 dependencies; its torch extensions JIT-build for sm_100 into
-baseline/_ref_build on first use). These tests run it through its public API
+baseline/_ref_build on first use; the fixture builds them in parallel, about
+a minute and a half on a fresh tree). These tests run it through its public API
 beside this library and require relative L2 <= 1e-5 between the two fp32
 results, the bar the reference's own kernels must meet against each other.
 They skip when baseline/_ref is not installed.
@@ -25,11 +26,12 @@ TOL = 1e-5
 
 @pytest.fixture(scope="module")
 def ref():
-    os.environ.setdefault("XDG_CACHE_HOME", os.path.join(ROOT, "baseline", "_ref_build"))
-    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    from bench_reference_cuda import build_reference_extensions, prepare_reference_env
+    prepare_reference_env()
     if REF not in sys.path:
         sys.path.insert(0, REF)
     import cliffordcuda
+    build_reference_extensions()
     return cliffordcuda
 
 
@@ -62,6 +64,8 @@ CASES = [
     ("left_contract", 10, (1,) * 9 + (0,), 512),
     ("geom_prod", 8, (-1,) * 8, 1024),
     ("geom_prod", 5, (1, 1, 1, -1, 0), 4096),
+    ("geom_prod", 14, (1,) * 11 + (-1, -1, 0), 1),    # the reference's tiled fused path
+    ("left_contract", 12, (1,) * 11 + (-1,), 4),
 ]
 
 
