@@ -197,6 +197,30 @@ __device__ __forceinline__ void quadrant_product(float (&acc)[64], const float *
         }
 }
 
+// store_quadrant with the layout chosen at run time (the two layouts the
+// fused backward needs): J_MAJOR stores entry (i, j) at j * 8 + i.
+__device__ __forceinline__ void store_quadrant_rt(float *mat, int blk, bool j_major,
+                                                  const float (&r)[64]) {
+    float *base = mat + blk * kBlockFloats;
+    if (j_major) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                *reinterpret_cast<float4 *>(base + u * 8 + 4 * h) =
+                    make_float4(r[slot_ij(4 * h + 0, u)], r[slot_ij(4 * h + 1, u)],
+                                r[slot_ij(4 * h + 2, u)], r[slot_ij(4 * h + 3, u)]);
+    } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                *reinterpret_cast<float4 *>(base + u * 8 + 4 * h) =
+                    make_float4(r[slot_ij(u, 4 * h + 0)], r[slot_ij(u, 4 * h + 1)],
+                                r[slot_ij(u, 4 * h + 2)], r[slot_ij(u, 4 * h + 3)]);
+    }
+}
+
 // out = rho^-1(op(U) op(V)): FWD U = x, V = y; GRAD_A (x = b, y = g) U = g,
 // V = b transposed; GRAD_B (x = a, y = g) U = a transposed, V = g.
 // One buffer per warp; the load latency of one warp's batch is hidden by the
@@ -251,16 +275,19 @@ __global__ void __launch_bounds__(32)
         float *U = sm + p * kRowFloats;
         float *V = U + kRegion;
         float r[64];
-        gather(r, U, q, s_in, std::make_integer_sequence<int, 64>{});
-        __syncwarp();  // every lane of the product has read its U row
-        to_matrix3(r);
-        factor4(r, c_fwd);
-        store_quadrant<true, TU>(U, r4, c4, r);
-        gather(r, V, q, s_in, std::make_integer_sequence<int, 64>{});
-        __syncwarp();
-        to_matrix3(r);
-        factor4(r, c_fwd);
-        store_quadrant<false, TV>(V, r4, c4, r);
+        // U -> op(rho(U)) as the A operand, V -> op(rho(V)) as the B operand:
+        // one loop body (a single copy of the conversion code, see the fused
+        // backward kernel below)
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) {
+            float *R = t == 0 ? U : V;
+            gather(r, R, q, s_in, std::make_integer_sequence<int, 64>{});
+            __syncwarp();  // every lane of the product has read its row
+            to_matrix3(r);
+            factor4(r, c_fwd);
+            const bool trans = t == 0 ? TU : TV;
+            store_quadrant_rt(R, trans ? c4 * 2 + r4 : r4 * 2 + c4, t == 0 ? !TU : TV, r);
+        }
         __syncwarp();
         quadrant_product(r, U, V, r4, c4);
         __syncwarp();  // all reads of the matrices done before U is overwritten
@@ -277,21 +304,55 @@ __global__ void __launch_bounds__(32)
     if (lane == 0) bulk_wait_all();
 }
 
+// quadrant_product with A's layout chosen at run time.
+__device__ __forceinline__ void quadrant_product_rt(float (&acc)[64], const float *A,
+                                                    const float *B, int r4, int c4,
+                                                    bool a_rowmajor) {
+#pragma unroll
+    for (int s = 0; s < 64; ++s) acc[s] = 0.0f;
+#pragma unroll 1
+    for (int k4 = 0; k4 < 2; ++k4)
+#pragma unroll 2
+        for (int kp = 0; kp < 8; ++kp) {
+            float av[8];
+            const float *pa = A + (r4 * 2 + k4) * kBlockFloats;
+            if (a_rowmajor) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) av[i] = pa[kp + i * 8];
+            } else {
+                const float4 a0 = *reinterpret_cast<const float4 *>(pa + kp * 8);
+                const float4 a1 = *reinterpret_cast<const float4 *>(pa + kp * 8 + 4);
+                av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+                av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+            }
+            const float4 *pb =
+                reinterpret_cast<const float4 *>(B + (k4 * 2 + c4) * kBlockFloats + kp * 8);
+            const float4 b0 = pb[0], b1 = pb[1];
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[slot_ij(i, j)] = fmaf(av[i], bv[j], acc[slot_ij(i, j)]);
+        }
+}
+
 // Both backward sums in one pass over a, b, g (5 KB per product instead of 6 KB
-// for two launches): grad_b = rho^-1(rho(a)^T rho(g)) first, from a stored
-// transposed as A and g as B; then grad_a = rho^-1(rho(g) rho(b)^T), reading
-// the columns of rho(g) from the same row-major copy. Each region holds an
-// input row, then a matrix, then an output row.
+// for two launches), in two phases that run the same code:
+//   phase 0: a and g load; rho(a)^T (the A operand) and rho(g) (the B
+//            operand, row-major) are formed; grad_b = rho^-1(rho(a)^T rho(g));
+//   phase 1: b loads into a's region once grad_b has left it; rho(b)^T is
+//            formed; grad_a = rho^-1(rho(g) rho(b)^T), reading the columns of
+//            rho(g) from its row-major copy.
+// The phases and their input conversions are loops, not unrolled copies: the
+// eleven warps of an SM run at different points of the kernel, and one copy
+// of each piece keeps the instruction working set small. Two regions per
+// product: 11 CTAs per SM (against 8 with all three rows resident).
 __global__ void __launch_bounds__(32)
     gp_mat16_bwd_kernel(const float *__restrict__ a, const float *__restrict__ b,
                         const float *__restrict__ g, float *__restrict__ ga,
                         float *__restrict__ gb, int64_t batch, int64_t nbatches, int *err) {
     extern __shared__ __align__(16) float sm[];
-    // Two regions: a and g are loaded together; b is loaded into a's region
-    // once grad_b (written there) has been stored. Against three regions (all
-    // rows loaded at once) this exposes a second load per batch but fits 12
-    // warps per SM instead of 8, and measured 4.5% faster.
-    float *const RA = sm, *const RG = sm + kRegion, *const RB = sm;
+    float *const RA = sm, *const RG = sm + kRegion;
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + 2 * kRegion);
     const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
     const int r4 = q >> 1, c4 = r4 ^ (q & 1);
@@ -309,69 +370,51 @@ __global__ void __launch_bounds__(32)
     }
     const float c_fwd = r4 ? 1.0f : -1.0f;
     const float c_inv = r4 ? -1.0f : 1.0f;
+    float *const A = RA + p * kRowFloats, *const G = RG + p * kRowFloats;
     bool ok = true;
-    uint32_t ph = 0;  // completed phases of `full`
-    int64_t bt = blockIdx.x;
-    for (; bt < nbatches && ok; bt += gridDim.x) {
+    uint32_t ph_count = 0;  // completed phases of `full`
+    for (int64_t bt = blockIdx.x; bt < nbatches && ok; bt += gridDim.x) {
         const int64_t r0 = bt * 8;
         const int nv = (int)std::min<int64_t>(8, batch - r0);
-        if (lane == 0) {
-            bulk_wait_read<0>();  // the previous batch's stores have read the regions
-            mbar_arrive_expect_tx(full, (uint32_t)nv * 2048u);
-            for (int i = 0; i < nv; ++i) {
-                bulk_load(RA + i * kRowFloats, a + (r0 + i) * 256, 1024, full);
-                bulk_load(RG + i * kRowFloats, g + (r0 + i) * 256, 1024, full);
+#pragma unroll 1
+        for (int ph = 0; ph < 2; ++ph) {
+            if (lane == 0) {
+                bulk_wait_read<0>();  // earlier stores have read region A
+                mbar_arrive_expect_tx(full, (uint32_t)nv * (ph == 0 ? 2048u : 1024u));
+                for (int i = 0; i < nv; ++i) {
+                    bulk_load(RA + i * kRowFloats, (ph == 0 ? a : b) + (r0 + i) * 256, 1024, full);
+                    if (ph == 0) bulk_load(RG + i * kRowFloats, g + (r0 + i) * 256, 1024, full);
+                }
             }
-        }
-        ok = mbar_wait_bounded(full, ph++ & 1, err, 0x302);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        float *A = RA + p * kRowFloats, *B = RB + p * kRowFloats, *G = RG + p * kRowFloats;
-        float r[64];
-        gather(r, A, q, s_in, std::make_integer_sequence<int, 64>{});
-        __syncwarp();
-        to_matrix3(r);
-        factor4(r, c_fwd);
-        store_quadrant<true, true>(A, r4, c4, r);  // rho(a)^T as the A operand
-        gather(r, G, q, s_in, std::make_integer_sequence<int, 64>{});
-        __syncwarp();
-        to_matrix3(r);
-        factor4(r, c_fwd);
-        store_quadrant<false, false>(G, r4, c4, r);  // rho(g) as the B operand (row-major)
-        __syncwarp();
-        quadrant_product(r, A, G, r4, c4);
-        __syncwarp();
-        factor4(r, c_inv);
-        from_matrix3(r);
-        scatter(r, A, q, s_out, std::make_integer_sequence<int, 64>{});  // grad_b row
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-            for (int i = 0; i < nv; ++i) bulk_store(gb + (r0 + i) * 256, RA + i * kRowFloats, 1024);
-            bulk_commit();
-        }
-        if (lane == 0) {
-            bulk_wait_read<0>();  // grad_b has left region A
-            mbar_arrive_expect_tx(full, (uint32_t)nv * 1024u);
-            for (int i = 0; i < nv; ++i) bulk_load(RB + i * kRowFloats, b + (r0 + i) * 256, 1024, full);
-        }
-        ok = mbar_wait_bounded(full, ph++ & 1, err, 0x304);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        gather(r, B, q, s_in, std::make_integer_sequence<int, 64>{});
-        __syncwarp();
-        to_matrix3(r);
-        factor4(r, c_fwd);
-        store_quadrant<false, true>(B, r4, c4, r);  // rho(b)^T as the B operand
-        __syncwarp();
-        quadrant_product<true>(r, G, B, r4, c4);
-        __syncwarp();
-        factor4(r, c_inv);
-        from_matrix3(r);
-        scatter(r, B, q, s_out, std::make_integer_sequence<int, 64>{});  // grad_a row
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-            for (int i = 0; i < nv; ++i) bulk_store(ga + (r0 + i) * 256, RB + i * kRowFloats, 1024);
-            bulk_commit();
+            ok = mbar_wait_bounded(full, ph_count++ & 1, err, ph == 0 ? 0x302 : 0x304);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            float r[64];
+#pragma unroll 1
+            for (int t = 0; t < (ph == 0 ? 2 : 1); ++t) {
+                // phase 0: a -> rho(a)^T (A operand), g -> rho(g) (B operand);
+                // phase 1: b -> rho(b)^T (B operand)
+                float *R = t == 1 ? G : A;
+                gather(r, R, q, s_in, std::make_integer_sequence<int, 64>{});
+                __syncwarp();  // every lane of the product has read its row
+                to_matrix3(r);
+                factor4(r, c_fwd);
+                const bool trans = (t == 0);
+                store_quadrant_rt(R, trans ? c4 * 2 + r4 : r4 * 2 + c4, ph == 1, r);
+            }
+            __syncwarp();
+            quadrant_product_rt(r, ph == 0 ? A : G, ph == 0 ? G : A, r4, c4, ph == 1);
+            __syncwarp();  // all reads of the matrices done before A is overwritten
+            factor4(r, c_inv);
+            from_matrix3(r);
+            scatter(r, A, q, s_out, std::make_integer_sequence<int, 64>{});
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                float *out = ph == 0 ? gb : ga;
+                for (int i = 0; i < nv; ++i)
+                    bulk_store(out + (r0 + i) * 256, RA + i * kRowFloats, 1024);
+                bulk_commit();
+            }
         }
     }
     if (lane == 0) bulk_wait_all();
