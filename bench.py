@@ -198,6 +198,10 @@ def main():
                     help="skip timing the blade-by-blade kernels beside the headline")
     ap.add_argument("--batch", type=int, default=None,
                     help="rows per GPU (profiling runs use a smaller case)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip measuring BASELINE configs 2-5 beside the headline")
+    ap.add_argument("--config-steps", type=int, default=10,
+                    help="timed steps of each config measurement in the default run")
     ap.add_argument("--workload", default="headline",
                     choices=["headline", "products", "layer", "rotor", "pga"],
                     help="headline = the BASELINE metric; the others measure configs 2-5")
@@ -308,6 +312,18 @@ def main():
             if not torch.equal(h, d.cpu()):
                 raise RuntimeError("e2e results differ from the device-resident results")
 
+    configs = None
+    if not args.no_configs:
+        # BASELINE configs 2-5 on the same GPUs and process group, each with
+        # the headline's timing rules (bench_configs.py); their full-length
+        # runs are `bench.py --workload products|layer|rotor|pga`.
+        import argparse as _ap
+        import bench_configs
+        del c, ga, gb
+        torch.cuda.empty_cache()
+        cargs = _ap.Namespace(steps=min(args.config_steps, K), warmup=args.warmup, batch=None)
+        configs = bench_configs.collect(cargs, world, rank, dev)
+
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline:
@@ -352,6 +368,7 @@ def main():
                     / (3 * D * 4)},
             "gpu_launches": 2 * K,
             "clocks": clk.summary(),
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

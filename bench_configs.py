@@ -64,6 +64,28 @@ def nnz_table(op, n, metric):
     return int(valid.sum())
 
 
+class CollectiveClock:
+    """CUDA events around the gradient all-reduce inside timed steps: its mean
+    time per step, to state the collective's share of the step."""
+
+    def __init__(self, stream):
+        self.stream, self.pairs = stream, []
+
+    def allreduce(self, module):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        allreduce_grads(module)
+        e1.record(self.stream)
+        self.pairs.append((e0, e1))
+
+    def mean_ms(self, last):
+        pairs = self.pairs[-last:] if last else []
+        if not pairs:
+            return None
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in pairs)
+
+
 class Timer:
     def __init__(self, dev, world):
         self.dev, self.world = dev, world
@@ -155,6 +177,8 @@ def layer(args, world, rank, dev, T):
         with torch.no_grad():
             lay.weight.copy_(torch.randn(1, D, device=dev, generator=gen) / math.sqrt(D))
 
+        cc_clock = CollectiveClock(T.stream)
+
         def step():
             lay.weight.grad = None
             x.grad = None
@@ -163,13 +187,16 @@ def layer(args, world, rank, dev, T):
             else:
                 y = lay(x)
             y.backward(dy)
-            allreduce_grads(lay)
+            cc_clock.allreduce(lay)
         ms, clk = T.time(step, args.steps, args.warmup)
+        ar_ms = cc_clock.mean_ms(args.steps) if world > 1 else None
         useful = 3 * 2 * B * D * D
         matrix_route = name == "gp"
         res[name] = {"route": "16x16 matrix representation (cb_layer_gp8_*)" if matrix_route
                      else "3xTF32 tcgen05 GEMM (cb_layer_*)",
                      "rows_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
+                     "allreduce_ms_per_step": ar_ms,
+                     "allreduce_share": None if ar_ms is None else ar_ms / ms,
                      "hbm_gbs": 6 * D * 4 * B / (ms / 1e3) / 1e9 if matrix_route
                      else 5 * D * 4 * B / (ms / 1e3) / 1e9}
         if not matrix_route:
@@ -216,13 +243,16 @@ def rotor(args, world, rank, dev, T):
     g = torch.randn(B, D, device=dev, generator=gen)
     lay.train()
 
+    cc_clock = CollectiveClock(T.stream)
+
     def step():
         lay.bivector.grad = None
         x.grad = None
         y = lay(x)
         y.backward(g)
-        allreduce_grads(lay)
+        cc_clock.allreduce(lay)
     ms, clk = T.time(step, args.steps, args.warmup)
+    ar_ms = cc_clock.mean_ms(args.steps) if world > 1 else None
     lay.eval()
     xe = x.detach()
 
@@ -246,6 +276,8 @@ def rotor(args, world, rank, dev, T):
     return _line(args, world, "Cl(7,1) RotorLayer training rows/s", world * B / (ms / 1e3),
                  "rows/s", ms, clk, cfg,
                  {"roofline": roof,
+                  "allreduce_ms_per_step": ar_ms,
+                  "allreduce_share": None if ar_ms is None else ar_ms / ms,
                   "eval": {"rows_per_s": world * B / (ms_eval / 1e3), "ms": ms_eval,
                            "hbm_gbs": eval_bytes / (ms_eval / 1e3) / 1e9,
                            "frac_hbm": eval_bytes / (ms_eval / 1e3) / 1e9 / HBM_GBS},
@@ -288,13 +320,31 @@ def pga(args, world, rank, dev, T):
                  "products/s", total, clk, cfg, {"ops": res})
 
 
+WORKLOADS = {"products": products, "layer": layer, "rotor": rotor, "pga": pga}
+
+
+def collect(args, world, rank, dev):
+    """Every config workload on an initialised device (and process group when
+    world > 1); {workload: line, or {"error": ...}}. Used by bench.py's
+    default run so that configs 2-5 are measured beside the headline."""
+    T = Timer(dev, world)
+    out = {}
+    for name, fn in WORKLOADS.items():
+        try:
+            out[name] = fn(args, world, rank, dev, T)
+        except Exception as e:  # reported in the line, the headline still prints
+            out[name] = {"error": repr(e)[:300]}
+        torch.cuda.empty_cache()
+    return out
+
+
 def run(args, world, rank, local):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
     T = Timer(dev, world)
-    fn = {"products": products, "layer": layer, "rotor": rotor, "pga": pga}[args.workload]
+    fn = WORKLOADS[args.workload]
     line = fn(args, world, rank, dev, T)
     from cliffordcuda_b200 import _lib
     _lib.device_status(dev)
