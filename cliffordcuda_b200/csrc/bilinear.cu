@@ -181,7 +181,7 @@ bool use_tiled(int op, int n, uint32_t neg, uint32_t zero, const void *x, const 
                const void *o, int64_t batch) {
     if (op == CB_OP_REG) return false;
     if (n < 5 || n > 10) return false;
-    if ((neg | zero) & 31u) return false;  // low five generators Euclidean
+    if (zero & 31u) return false;  // no null generator among the low five
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
     if (!al(x) || !al(y) || !al(o)) return false;
     if ((uint64_t)batch * (1u << n) / 32 >= (1ull << 31)) return false;

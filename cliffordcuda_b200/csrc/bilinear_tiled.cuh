@@ -79,8 +79,16 @@ __host__ __device__ constexpr int reorderl(int p, int q) {
     return c & 1;
 }
 
-// Coefficient of x[i_l] * y[i_l ^ k_l] in output k_l for the low block.
-template <int MODE, int OPK>
+// Low generators that square to -1: NEGL of them, relabelled (see
+// LowRelabel) to the top NEGL bits of the low block, so that the low block's
+// metric is a compile-time pattern.
+__host__ __device__ constexpr int low_neg_mask(int negl) {
+    return ((1 << negl) - 1) << (kLow - negl);
+}
+
+// Coefficient of x[i_l] * y[i_l ^ k_l] in output k_l for the low block:
+// reordering sign times the low metric over P_l & Q_l times the predicate.
+template <int MODE, int OPK, int NEGL = 0>
 __host__ __device__ constexpr int low_coef(int il, int kl) {
     const int jl = il ^ kl;
     const int P = (MODE == CB_MODE_GRAD_A) ? kl : il;
@@ -90,7 +98,7 @@ __host__ __device__ constexpr int low_coef(int il, int kl) {
                    : (OPK == OPK_LC)    ? ((P & ~Q & (kBlk - 1)) == 0)
                                         : ((Q & ~P & (kBlk - 1)) == 0);
     if (!m) return 0;
-    return reorderl(P, Q) ? -1 : 1;
+    return (reorderl(P, Q) ^ (popcl(P & Q & low_neg_mask(NEGL)) & 1)) ? -1 : 1;
 }
 
 // Coefficient table of one body variant, evaluated by the compiler's
@@ -99,40 +107,80 @@ struct CoefTable {
     signed char c[kBlk * kBlk];
 };
 
-template <int MODE, int OPK>
+template <int MODE, int OPK, int NEGL>
 __host__ __device__ constexpr CoefTable make_coefs() {
     CoefTable t{};
-    for (int i = 0; i < kBlk * kBlk; ++i) t.c[i] = (signed char)low_coef<MODE, OPK>(i / kBlk, i % kBlk);
+    for (int i = 0; i < kBlk * kBlk; ++i)
+        t.c[i] = (signed char)low_coef<MODE, OPK, NEGL>(i / kBlk, i % kBlk);
     return t;
 }
 
-template <int MODE, int OPK>
+template <int MODE, int OPK, int NEGL>
 struct Coefs {
-    static constexpr CoefTable table = make_coefs<MODE, OPK>();
+    static constexpr CoefTable table = make_coefs<MODE, OPK, NEGL>();
 };
 
-template <int MODE, int OPK, int I>
+template <int MODE, int OPK, int NEGL, int I>
 __device__ __forceinline__ void fma_term(float (&acc)[kBlk], const float (&xv)[kBlk],
                                          const float (&yv)[kBlk]) {
     constexpr int il = I / kBlk, kl = I % kBlk;
-    constexpr int c = Coefs<MODE, OPK>::table.c[I];
+    constexpr int c = Coefs<MODE, OPK, NEGL>::table.c[I];
     if constexpr (c > 0) acc[kl] = fmaf(xv[il], yv[il ^ kl], acc[kl]);
     else if constexpr (c < 0) acc[kl] = fmaf(-xv[il], yv[il ^ kl], acc[kl]);
 }
 
-template <int MODE, int OPK, int... I>
+template <int MODE, int OPK, int NEGL, int... I>
 __device__ __forceinline__ void block_fma_seq(float (&acc)[kBlk], const float (&xv)[kBlk],
                                               const float (&yv)[kBlk],
                                               std::integer_sequence<int, I...>) {
-    (fma_term<MODE, OPK, I>(acc, xv, yv), ...);
+    (fma_term<MODE, OPK, NEGL, I>(acc, xv, yv), ...);
 }
 
 // acc[k_l] += c(i_l, k_l) x[i_l] y[i_l ^ k_l] over the block, i_l outer.
-template <int MODE, int OPK>
+template <int MODE, int OPK, int NEGL = 0>
 __device__ __forceinline__ void block_fma(float (&acc)[kBlk], const float (&xv)[kBlk],
                                           const float (&yv)[kBlk]) {
-    block_fma_seq<MODE, OPK>(acc, xv, yv, std::make_integer_sequence<int, kBlk * kBlk>{});
+    block_fma_seq<MODE, OPK, NEGL>(acc, xv, yv, std::make_integer_sequence<int, kBlk * kBlk>{});
 }
+
+// Relabelling of the five low generators that moves the ones squaring to -1
+// to the top bits of the low block (positives keep their order below them).
+// Within each 128-byte line the coefficient of blade i_l moves to to_new[i_l]
+// and changes sign when the reordering of its generators is odd (bit i_l of
+// eps); results move back through to_old. Identity when inactive.
+struct LowRelabel {
+    unsigned char to_new[kBlk];
+    unsigned char to_old[kBlk];
+    uint32_t eps;
+    int active;
+};
+
+inline LowRelabel make_relabel(uint32_t negL) {
+    LowRelabel r{};
+    int pos[kLow];
+    int next = 0;
+    for (int b = 0; b < kLow; ++b)
+        if (!((negL >> b) & 1)) pos[b] = next++;
+    for (int b = 0; b < kLow; ++b)
+        if ((negL >> b) & 1) pos[b] = next++;
+    r.active = 0;
+    for (int b = 0; b < kLow; ++b) r.active |= pos[b] != b;
+    r.eps = 0;
+    for (int il = 0; il < kBlk; ++il) {
+        int nw = 0, inv = 0;
+        for (int a = 0; a < kLow; ++a) {
+            if (!((il >> a) & 1)) continue;
+            nw |= 1 << pos[a];
+            for (int b = a + 1; b < kLow; ++b)
+                if (((il >> b) & 1) && pos[a] > pos[b]) ++inv;
+        }
+        r.to_new[il] = (unsigned char)nw;
+        r.to_old[nw] = (unsigned char)il;
+        if (inv & 1) r.eps |= 1u << il;
+    }
+    return r;
+}
+
 
 // Swizzled shared tile: float f of the tile lives in 128-byte line f >> 5, in
 // 16-byte chunk ((f >> 2) & 7) ^ (line & 7) -- the TMA 128B swizzle pattern.
@@ -162,6 +210,32 @@ __device__ __forceinline__ void store_block(float *tile, int line, const float (
 __device__ __forceinline__ int swz_index(int f) {
     const int line = f >> 5;
     return line * 32 + ((((f >> 2) & 7) ^ (line & 7)) << 2) + (f & 3);
+}
+
+// Offset of float e of line `line` within a swizzled tile.
+__device__ __forceinline__ int swz_off(int line, int e) {
+    return line * 32 + ((((e >> 2) & 7) ^ (line & 7)) << 2) + (e & 3);
+}
+
+// In place on line `line` of a swizzled tile: x'[to_new[i]] = eps(i) x[i].
+__device__ __forceinline__ void relabel_line(float *tile, int line, const LowRelabel &rl) {
+    float v[kBlk];
+#pragma unroll
+    for (int e = 0; e < kBlk; ++e) v[e] = tile[swz_off(line, e)];
+#pragma unroll
+    for (int e = 0; e < kBlk; ++e)
+        tile[swz_off(line, rl.to_new[e])] = ((rl.eps >> e) & 1) ? -v[e] : v[e];
+}
+
+// Store this thread's 32 sums (relabelled order) into line `line` in the
+// caller's order: out[i] = eps(i) acc[to_new[i]], i.e. acc[r] goes to to_old[r].
+__device__ __forceinline__ void store_block_relabel(float *tile, int line, const float (&acc)[kBlk],
+                                                    const LowRelabel &rl) {
+#pragma unroll
+    for (int r = 0; r < kBlk; ++r) {
+        const int o = rl.to_old[r];
+        tile[swz_off(line, o)] = ((rl.eps >> o) & 1) ? -acc[r] : acc[r];
+    }
 }
 
 __device__ __forceinline__ void apply_sign(float (&yv)[kBlk], float2 sg) {
@@ -197,7 +271,7 @@ __host__ __device__ inline size_t smem_bytes(int n, bool inner) {
            table_entries(n, inner) * sizeof(float2) + 64;
 }
 
-template <int MODE, int OPK>
+template <int MODE, int OPK, int NEGL>
 __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const float *yt,
                                       const float2 *tab, const float2 *tab2, int rowl, int kh,
                                       int lgNH, bool skip_zero) {
@@ -230,21 +304,30 @@ __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const
             for (int e = 0; e < kBlk; ++e) y2[e] = yv[e];
             apply_sign(yv, sg);
             apply_sign(y2, sg2);
-            block_fma<MODE, OPK_LC>(acc, xv, yv);
-            block_fma<MODE, OPK_RC>(acc, xv, y2);
+            block_fma<MODE, OPK_LC, NEGL>(acc, xv, yv);
+            block_fma<MODE, OPK_RC, NEGL>(acc, xv, y2);
         } else {
             apply_sign(yv, sg);
-            block_fma<MODE, OPK>(acc, xv, yv);
+            block_fma<MODE, OPK, NEGL>(acc, xv, yv);
         }
     }
 }
 
-template <int MODE, int OPK>
+// Sign s_L(e, e) (-1)^(popc(k_h) popc(e)) of the diagonal term e of line k_h
+// (the inner product's correction).
+template <int NEGL>
+__device__ __forceinline__ int diag_sign(int e, int kh) {
+    return (reorderl(e, e) ^ (popcl(e & low_neg_mask(NEGL)) & 1) ^ ((popcl(e) & 1) & parity(kh)))
+               ? -1 : 1;
+}
+
+template <int MODE, int OPK, int NEGL>
 __global__ void __launch_bounds__(kThreads, 3)
     bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
                           const __grid_constant__ CUtensorMap my,
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
-                          uint32_t zero, int num_tiles, int *err, bool skip_zero) {
+                          uint32_t zero, int num_tiles, int *err, bool skip_zero,
+                          const LowRelabel rl) {
     extern __shared__ unsigned char smem_raw[];
     // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
@@ -309,12 +392,17 @@ __global__ void __launch_bounds__(kThreads, 3)
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / kStages) & 1, err, 0x101)))
             break;
         float *xt = xs + s * kTileFloats;
-        const float *yt = ys + s * kTileFloats;
+        float *yt = ys + s * kTileFloats;
+        if (rl.active) {  // the row's lines move to the relabelled low order
+            relabel_line(xt, rowl + kh, rl);
+            relabel_line(yt, rowl + kh, rl);
+            __syncwarp();  // a row's lines are read by the row's threads, one warp
+        }
 
         float acc[kBlk];
 #pragma unroll
         for (int e = 0; e < kBlk; ++e) acc[e] = 0.0f;
-        sweep<MODE, OPK>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
+        sweep<MODE, OPK, NEGL>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
 
         if (MODE == CB_MODE_GRAD_A && parity(kh)) {
 #pragma unroll
@@ -332,26 +420,25 @@ __global__ void __launch_bounds__(kThreads, 3)
                 load_block(yt, rowl + kh, yv);
                 float dpart = 0.0f;
 #pragma unroll
-                for (int e = 0; e < kBlk; ++e) {
-                    const int sl = (reorderl(e, e) ^ ((popcl(e) & 1) & parity(kh))) ? -1 : 1;
-                    dpart = fmaf((float)(shh * sl) * xv[e], yv[e], dpart);
-                }
+                for (int e = 0; e < kBlk; ++e)
+                    dpart = fmaf((float)(shh * diag_sign<NEGL>(e, kh)) * xv[e], yv[e], dpart);
                 // the row's NH threads are consecutive lanes of one warp
                 for (int m = 1; m < NH; m <<= 1) dpart += __shfl_xor_sync(0xffffffffu, dpart, m);
                 if (kh == 0) acc[0] -= dpart;
             } else {  // out[k] -= s(k, k) x_k y_0
                 const float y0 = yt[swz_index(rowl << 5)];
 #pragma unroll
-                for (int e = 0; e < kBlk; ++e) {
-                    const int sl = (reorderl(e, e) ^ ((popcl(e) & 1) & parity(kh))) ? -1 : 1;
-                    acc[e] = fmaf(-(float)(shh * sl) * xv[e], y0, acc[e]);
-                }
+                for (int e = 0; e < kBlk; ++e)
+                    acc[e] = fmaf(-(float)(shh * diag_sign<NEGL>(e, kh)) * xv[e], y0, acc[e]);
             }
         }
         // This warp's rows are read only by this warp: once its lanes are done
         // reading, the results can replace the x values of those rows.
         __syncwarp();
-        store_block(xt, rowl + kh, acc);
+        if (rl.active)
+            store_block_relabel(xt, rowl + kh, acc, rl);
+        else
+            store_block(xt, rowl + kh, acc);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -376,9 +463,9 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (lane == 0) bulk_wait_all();
 }
 
-template <int MODE, int OPK>
-int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int n, uint32_t neg,
-                 uint32_t zero, cudaStream_t stream) {
+template <int MODE, int OPK, int NEGL>
+int launch_tiled_k(const float *x, const float *y, float *out, int64_t batch, int n, uint32_t neg,
+                   uint32_t zero, const LowRelabel &rl, cudaStream_t stream) {
     DeviceInfo di;
     int st = device_info(&di);
     if (st) return st;
@@ -391,7 +478,7 @@ int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int 
     if ((st = make_tmap_lines(&my, y, lines, kTileLines))) return st;
     if ((st = make_tmap_lines(&mo, out, lines, kTileLines))) return st;
     const size_t smem = smem_bytes(n, OPK == OPK_INNER);
-    auto kern = bilinear_tiled_kernel<MODE, OPK>;
+    auto kern = bilinear_tiled_kernel<MODE, OPK, NEGL>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bilinear_tiled)");
@@ -410,10 +497,38 @@ int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int 
     }
     const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * di.sm_count);
     const bool skip_zero = n >= 9 || (zero >> kLow) != 0;
-    kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err, skip_zero);
+    kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err, skip_zero,
+                                           rl);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "launch bilinear_tiled_kernel");
     return CB_OK;
+}
+
+// Low generators squaring to -1 are relabelled to the top of the low block
+// and served by the body compiled for their count; the wedge product never
+// meets the metric (P & Q = 0), so it keeps the Euclidean body.
+template <int MODE, int OPK>
+int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int n, uint32_t neg,
+                 uint32_t zero, cudaStream_t stream) {
+    if constexpr (OPK == OPK_WEDGE) {
+        const uint32_t negh = neg & ~(uint32_t)(kBlk - 1);
+        return launch_tiled_k<MODE, OPK, 0>(x, y, out, batch, n, negh, zero, make_relabel(0),
+                                            stream);
+    } else {
+        const uint32_t negL = neg & (kBlk - 1);
+        const int negl = __builtin_popcount(negL);
+        const LowRelabel rl = make_relabel(negL);
+        // the relabelled metric: low negatives on the top bits
+        const uint32_t negr = (neg & ~(uint32_t)(kBlk - 1)) | (uint32_t)low_neg_mask(negl);
+        switch (negl) {
+        case 0: return launch_tiled_k<MODE, OPK, 0>(x, y, out, batch, n, negr, zero, rl, stream);
+        case 1: return launch_tiled_k<MODE, OPK, 1>(x, y, out, batch, n, negr, zero, rl, stream);
+        case 2: return launch_tiled_k<MODE, OPK, 2>(x, y, out, batch, n, negr, zero, rl, stream);
+        case 3: return launch_tiled_k<MODE, OPK, 3>(x, y, out, batch, n, negr, zero, rl, stream);
+        case 4: return launch_tiled_k<MODE, OPK, 4>(x, y, out, batch, n, negr, zero, rl, stream);
+        default: return launch_tiled_k<MODE, OPK, 5>(x, y, out, batch, n, negr, zero, rl, stream);
+        }
+    }
 }
 
 }  // namespace tiled

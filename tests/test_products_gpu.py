@@ -225,3 +225,20 @@ def test_direct_path_cl8_gp():
         m = bilinear_raw("gp", mode, x, y, n, metric)
         assert rel_l2(d.cpu().numpy(), r) <= REL_L2_TOL, mode
         assert rel_l2(d.cpu().numpy(), m.cpu().numpy()) < 1e-6, mode
+
+
+@pytest.mark.parametrize("metric", [
+    (-1,) * 8,                                  # Cl(0,8): every low generator negative
+    (1, 1, 1, 1, -1, -1, -1, -1),               # Cl(4,4): one negative low generator
+    (1, -1, 1, -1, 1, -1, 1, -1, 1, -1),        # alternating: negatives relabelled
+    (-1, 1, 1, -1, 1, 1, -1),                   # Cl(4,3), negatives at low bits 0 and 3
+    (1, 1, -1, 1, 1, 0, -1, 1, 1),              # a null generator among the high bits
+])
+@pytest.mark.parametrize("op", ["gp", "wedge", "inner", "lc", "rc"])
+def test_negative_low_generators_tiled(op, metric):
+    """Metrics with generators squaring to -1 among the low five run the tiled
+    kernel (the negatives relabelled to the top of the low block); aligned
+    (tiled) against the oracle, and against the unaligned (generic) path."""
+    n = len(metric)
+    _check_all_modes(op, n, metric, 67, seed=n + len(op))
+    _check_all_modes(op, n, metric, 19, seed=n + 1, offset=1)
