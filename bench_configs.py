@@ -285,7 +285,7 @@ def rotor(args, world, rank, dev, T):
 
 
 def pga(args, world, rank, dev, T):
-    from cliffordcuda_b200.products import bilinear_raw
+    from cliffordcuda_b200.products import bilinear_bwd_raw, bilinear_raw
     n, metric = 10, (1,) * 9 + (0,)
     D = 1 << n
     B = args.batch or (131_072 // world)
@@ -301,16 +301,21 @@ def pga(args, world, rank, dev, T):
     total = 0.0
     for op in ("gp", "lc"):
         def step():
+            # the two native calls of the public API's autograd: the forward
+            # and both backward sums (cb_bilinear_bwd*)
             bilinear_raw(op, "fwd", a, b, n, metric, out=outs[0])
-            bilinear_raw(op, "grad_a", b, g, n, metric, out=outs[1])
-            bilinear_raw(op, "grad_b", a, g, n, metric, out=outs[2])
+            bilinear_bwd_raw(op, a, b, g, n, metric, outs[1], outs[2])
         ms, clk = T.time(step, args.steps, args.warmup)
         total += ms
         flops = 3 * 2 * nnz_table(op, n, metric) * B
-        bytes_ = 9 * D * 4 * B
-        res[op] = {"products_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
+        bytes_ = 8 * D * 4 * B  # forward: a, b, c; backward: a, b, g, grad_a, grad_b
+        res[op] = {"route": "dual numbers over Cl(9,0) = Cl(8,0) + Cl(8,0): six 16x16 matrix "
+                            "products per sum (cb_bilinear_ws)" if op == "gp" else
+                            "tiled blade-by-blade kernel",
+                   "products_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
                    "fp32_tflops": flops / (ms / 1e3) / 1e12,
-                   "pct_fp32_peak": 100 * flops / (ms / 1e3) / 1e12 / fp32_peak_tflops(dev),
+                   ("blade_flop_equivalent_pct" if op == "gp" else "pct_fp32_peak"):
+                       100 * flops / (ms / 1e3) / 1e12 / fp32_peak_tflops(dev),
                    "hbm_gbs": bytes_ / (ms / 1e3) / 1e9,
                    "pct_hbm": 100 * bytes_ / (ms / 1e3) / 1e9 / HBM_GBS}
     cfg = {"workload": "config 5: Cl(9,0,1) gp and lc fwd+bwd, 10% rows even-versor",

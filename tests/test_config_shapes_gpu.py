@@ -137,7 +137,10 @@ def test_config5_even_versor_rows(op):
         err = rel_l2(out[rows].cpu().numpy(), ref)
         assert err <= REL_L2_TOL, f"{op} {mode}: rel L2 {err:.3e}"
         if mode == "fwd" and op == "gp":
+            # an even versor times an even versor is even: the odd grades of
+            # those rows vanish (to fp32 rounding on the matrix-representation route)
             odd = (grades % 2 == 1)
-            assert torch.count_nonzero(out[sparse][:, odd]).item() == 0
+            ev = out[sparse]
+            assert ev[:, odd].abs().max().item() <= 1e-5 * ev.abs().max().item()
         del out
     _lib.device_status(DEV)

@@ -242,3 +242,19 @@ def test_negative_low_generators_tiled(op, metric):
     n = len(metric)
     _check_all_modes(op, n, metric, 67, seed=n + len(op))
     _check_all_modes(op, n, metric, 19, seed=n + 1, offset=1)
+
+
+@pytest.mark.parametrize("batch", [1, 5, 333])
+def test_pga10_route(batch):
+    """The Cl(9,0,1) geometric product goes through six Cl(8,0) matrix
+    products per sum (cb_bilinear_ws / cb_bilinear_bwd_ws); against the oracle,
+    and against the blade-by-blade kernels (cb_bilinear_direct)."""
+    n, metric = 10, (1,) * 9 + (0,)
+    a, b, g = inputs(n, 40 + batch, batch)
+    ref = O.forward_backward("gp", n, metric, a, b, g)
+    got = fwd_bwd_gpu("gp", metric, a, b, g)
+    for mine, r, name in zip(got, ref, ("c", "ga", "gb")):
+        assert rel_l2(mine, r) <= REL_L2_TOL, name
+    ta, tb = torch.tensor(a, device=DEV), torch.tensor(b, device=DEV)
+    d = bilinear_raw("gp", "fwd", ta, tb, n, metric, direct=True)
+    assert rel_l2(got[0], d.cpu().numpy()) < 1e-6
