@@ -179,7 +179,6 @@ int launch_generic(int op, const float *x, const float *y, float *out, int64_t b
 
 bool use_tiled(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
                const void *o, int64_t batch) {
-    if (op == CB_OP_REG) return false;
     if (n < 5 || n > 10) return false;
     if (zero & 31u) return false;  // no null generator among the low five
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };

@@ -63,7 +63,7 @@ constexpr int kTileLines = kTileFloats / 32;  // 128 lines of 128 bytes
 constexpr int kTileBytes = kTileFloats * 4;
 constexpr int kStages = 2;                    // tiles in flight per CTA
 
-enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4 };
+enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4, OPK_REG = 5 };
 
 __host__ __device__ constexpr int popcl(int v) {
     int c = 0;
@@ -238,6 +238,23 @@ __device__ __forceinline__ void store_block_relabel(float *tile, int line, const
     }
 }
 
+// The regressive product is dual o wedge o dual (the dual x I^-1 is a signed
+// reversal of a row). Its dual steps move line L of a row to line NH-1-L,
+// float e to 31 - e, with the factor I^2 (-1)^popc(P & dmask) of P = the source
+// blade index (comp = false) or its complement (comp = true), where
+// dmask = odd positions xor the negative generators: e_P I = that factor
+// times e_~P up to the I^2 of I^-1.
+__device__ __forceinline__ void dual_move(const float (&v)[kBlk], float *tile, int dst_line,
+                                          uint32_t src_base, uint32_t full, uint32_t dmask,
+                                          float isq, bool comp) {
+#pragma unroll
+    for (int e = 0; e < kBlk; ++e) {
+        const uint32_t P = comp ? (full ^ (src_base + e)) : (src_base + e);
+        const float f = (__popc(P & dmask) & 1) ? -isq : isq;
+        tile[swz_off(dst_line, kBlk - 1 - e)] = f * v[e];
+    }
+}
+
 __device__ __forceinline__ void apply_sign(float (&yv)[kBlk], float2 sg) {
 #pragma unroll
     for (int e = 0; e < kBlk; ++e) yv[e] *= (popcl(e) & 1) ? sg.y : sg.x;
@@ -337,6 +354,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int lgNH = n - kLow;
     const int NH = 1 << lgNH;
     constexpr bool inner = (OPK == OPK_INNER);
+    constexpr bool reg = (OPK == OPK_REG);
+    constexpr int OPB = reg ? OPK_WEDGE : OPK;  // the sweep's product
     float2 *tab = reinterpret_cast<float2 *>(ys + kStages * kTileFloats);
     float2 *tab2 = tab + NH * NH;
     uint64_t *bars = reinterpret_cast<uint64_t *>(tab + table_entries(n, inner));
@@ -364,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 3)
             tab[e] = high_factor(MODE, OPK_LC, ih, k, negH, zeroH);
             tab2[e] = high_factor(MODE, OPK_RC, ih, k, negH, zeroH);
         } else {
-            tab[e] = high_factor(MODE, OPK, ih, k, negH, zeroH);
+            tab[e] = high_factor(MODE, OPB, ih, k, negH, zeroH);
         }
     }
     __syncthreads();
@@ -398,11 +417,24 @@ __global__ void __launch_bounds__(kThreads, 3)
             relabel_line(yt, rowl + kh, rl);
             __syncwarp();  // a row's lines are read by the row's threads, one warp
         }
+        const uint32_t allb = (uint32_t)D - 1;  // the pseudoscalar's blade
+        const uint32_t dmask = (0xAAAAAAAAu ^ neg) & allb;
+        const float isq = reg ? (float)blade_sign(allb, allb, neg, zero) : 1.0f;  // I^2 = 1/I^2
+        if (reg) {  // x' = D x; y' = D b (forward) or D^T g (backward sums)
+            float xv[kBlk], yv[kBlk];
+            load_block(xt, rowl + kh, xv);
+            load_block(yt, rowl + kh, yv);
+            __syncwarp();
+            dual_move(xv, xt, rowl + NH - 1 - kh, (uint32_t)kh * kBlk, allb, dmask, isq, false);
+            dual_move(yv, yt, rowl + NH - 1 - kh, (uint32_t)kh * kBlk, allb, dmask, isq,
+                      MODE != CB_MODE_FWD);
+            __syncwarp();
+        }
 
         float acc[kBlk];
 #pragma unroll
         for (int e = 0; e < kBlk; ++e) acc[e] = 0.0f;
-        sweep<MODE, OPK, NEGL>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
+        sweep<MODE, OPB, NEGL>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
 
         if (MODE == CB_MODE_GRAD_A && parity(kh)) {
 #pragma unroll
@@ -435,7 +467,10 @@ __global__ void __launch_bounds__(kThreads, 3)
         // This warp's rows are read only by this warp: once its lanes are done
         // reading, the results can replace the x values of those rows.
         __syncwarp();
-        if (rl.active)
+        if (reg)  // out = D t (forward) or D^T t (backward sums)
+            dual_move(acc, xt, rowl + NH - 1 - kh, (uint32_t)kh * kBlk, allb, dmask, isq,
+                      MODE != CB_MODE_FWD);
+        else if (rl.active)
             store_block_relabel(xt, rowl + kh, acc, rl);
         else
             store_block(xt, rowl + kh, acc);
@@ -514,6 +549,9 @@ int launch_tiled(const float *x, const float *y, float *out, int64_t batch, int 
         const uint32_t negh = neg & ~(uint32_t)(kBlk - 1);
         return launch_tiled_k<MODE, OPK, 0>(x, y, out, batch, n, negh, zero, make_relabel(0),
                                             stream);
+    } else if constexpr (OPK == OPK_REG) {  // wedge body; the dual steps read the full metric
+        return launch_tiled_k<MODE, OPK, 0>(x, y, out, batch, n, neg, zero, make_relabel(0),
+                                            stream);
     } else {
         const uint32_t negL = neg & (kBlk - 1);
         const int negl = __builtin_popcount(negL);
@@ -544,6 +582,7 @@ int bilinear_tiled(int op, const float *x, const float *y, float *out, int64_t b
     case CB_OP_LC: return launch_tiled<MODE, OPK_LC>(x, y, out, batch, n, neg, zero, stream);
     case CB_OP_RC: return launch_tiled<MODE, OPK_RC>(x, y, out, batch, n, neg, zero, stream);
     case CB_OP_INNER: return launch_tiled<MODE, OPK_INNER>(x, y, out, batch, n, neg, zero, stream);
+    case CB_OP_REG: return launch_tiled<MODE, OPK_REG>(x, y, out, batch, n, neg, zero, stream);
     }
     set_error("op %d has no tiled kernel", op);
     return CB_ERR_INVALID;
