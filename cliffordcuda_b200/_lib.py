@@ -45,10 +45,6 @@ SIGNATURES = {
     "cb_rotor_apply_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _i64, _vp]),
     "cb_rotor_compile_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp]),
     "cb_rotor_apply_bwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
-    "cb_bilinear_workspace_bytes": (_i32, [_i32, _i32, _u32, _u32, _i64, ctypes.POINTER(_i64)]),
-    "cb_bilinear_ws": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp, _i64, _vp]),
-    "cb_bilinear_bwd_ws": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp,
-                                  _i64, _vp]),
     "cb_blade_map": (_i32, [_i32, _vp, _vp, _i64, _i32, _u32, _u32, _i32, _vp]),
     "cb_norm_sq": (_i32, [_vp, _vp, _i64, _i32, _u32, _u32, _vp]),
     "cb_norm_sq_bwd": (_i32, [_vp, _vp, _vp, _i64, _i32, _u32, _u32, _vp]),

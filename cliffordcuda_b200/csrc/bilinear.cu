@@ -246,6 +246,8 @@ int bilinear(int op, int mode, const float *x, const float *y, float *out, int64
     if (st || batch == 0) return st;
     if (!direct && use_mat16(op, n, neg, zero, x, y, out))
         return gp_mat16(mode, x, y, out, batch, stream);
+    if (!direct && use_pga10(op, n, neg, zero, x, y, out))
+        return pga10(mode, x, y, out, batch, stream);
     if (use_tiled(op, n, neg, zero, x, y, out, batch)) {
         switch (mode) {
         case CB_MODE_FWD:
@@ -323,58 +325,4 @@ extern "C" int cb_bilinear_bwd(int op, const float *a, const float *b, const flo
     if (grad_b)
         st = cb::bilinear(op, CB_MODE_GRAD_B, a, g, grad_b, batch, n, neg_mask, zero_mask, s);
     return st;
-}
-
-// ------------------------------------------------- entry points with workspace --
-extern "C" int cb_bilinear_workspace_bytes(int op, int n, uint32_t neg_mask, uint32_t zero_mask,
-                                           int64_t batch, int64_t *bytes) {
-    if (!bytes || batch < 0) {
-        cb::set_error("cb_bilinear_workspace_bytes: invalid arguments");
-        return CB_ERR_INVALID;
-    }
-    *bytes = cb::use_pga10(op, n, neg_mask, zero_mask) ? cb::pga10_workspace_bytes(batch) : 0;
-    return CB_OK;
-}
-
-extern "C" int cb_bilinear_ws(int op, int mode, const float *x, const float *y, float *out,
-                              int64_t batch, int n, uint32_t neg_mask, uint32_t zero_mask,
-                              void *workspace, int64_t workspace_bytes, void *stream) {
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (mode == CB_MODE_FWD && cb::use_pga10(op, n, neg_mask, zero_mask)) {
-        int st = cb::check_args(op, mode, x, y, out, batch, n, neg_mask, zero_mask);
-        if (st || batch == 0) return st;
-        return cb::pga10_fwd(x, y, out, batch, workspace, workspace_bytes, s);
-    }
-    // a single backward sum gets x = the other operand and y = the upstream
-    // gradient; the route's backward needs both operands, so it stays direct
-    return cb::bilinear(op, mode, x, y, out, batch, n, neg_mask, zero_mask, s);
-}
-
-extern "C" int cb_bilinear_bwd_ws(int op, const float *a, const float *b, const float *g,
-                                  float *grad_a, float *grad_b, int64_t batch, int n,
-                                  uint32_t neg_mask, uint32_t zero_mask, void *workspace,
-                                  int64_t workspace_bytes, void *stream) {
-    if (cb::use_pga10(op, n, neg_mask, zero_mask) && (grad_a || grad_b)) {
-        int st = CB_OK;
-        if (grad_a) st = cb::check_args(op, CB_MODE_GRAD_A, b, g, grad_a, batch, n, neg_mask,
-                                        zero_mask);
-        if (!st && grad_b)
-            st = cb::check_args(op, CB_MODE_GRAD_B, a, g, grad_b, batch, n, neg_mask, zero_mask);
-        if (!st && batch > 0) {
-            const void *outs[2] = {grad_a, grad_b};
-            for (const void *o : outs)
-                if (o && (o == a || o == b || o == g)) {
-                    cb::set_error("gradient outputs must not alias an input");
-                    return CB_ERR_INVALID;
-                }
-            if (grad_a && grad_a == grad_b) {
-                cb::set_error("grad_a and grad_b must be different buffers");
-                return CB_ERR_INVALID;
-            }
-        }
-        if (st || batch == 0) return st;
-        return cb::pga10_bwd(a, b, g, grad_a, grad_b, batch, workspace, workspace_bytes,
-                             static_cast<cudaStream_t>(stream));
-    }
-    return cb_bilinear_bwd(op, a, b, g, grad_a, grad_b, batch, n, neg_mask, zero_mask, stream);
 }

@@ -262,15 +262,14 @@ constexpr int kGpLayerWFloats = 288;
 int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, float *gb,
                  int64_t batch, cudaStream_t s);
 
-// Cl(9,0,1) geometric product through Cl(8,0) matrix products (pga10.cu):
-// applicable when use_pga10 holds; the caller's workspace holds the
-// intermediate Cl(8,0) planes (pga10_workspace_bytes).
-bool use_pga10(int op, int n, uint32_t neg, uint32_t zero);
-int64_t pga10_workspace_bytes(int64_t batch);
-int pga10_fwd(const float *a, const float *b, float *c, int64_t batch, void *ws,
-              int64_t ws_bytes, cudaStream_t s);
-int pga10_bwd(const float *a, const float *b, const float *g, float *ga, float *gb, int64_t batch,
-              void *ws, int64_t ws_bytes, cudaStream_t s);
+// Cl(9,0,1) geometric product through Cl(8,0) matrix products (pga10.cu),
+// applicable when use_pga10 holds; gp9 is one sum over Cl(9,0) blocks
+// (block h of 1024-float rows; g* = grade involution; acc = add into out).
+bool use_pga10(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
+               const void *o);
+int pga10(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s);
+int gp9(int mode, const float *x, int hx, int gx, const float *y, int hy, int gy, float *out,
+        int ho, int gout, int acc, int64_t batch, cudaStream_t s);
 
 // internal bilinear dispatcher (bilinear.cu)
 // direct: always the blade-by-blade kernels (never the matrix representation).

@@ -336,6 +336,187 @@ __device__ __forceinline__ void quadrant_product_rt(float (&acc)[64], const floa
         }
 }
 
+// ------------------------------------------------ Cl(9,0) blocks --
+// The same sums for Cl(9,0) = Cl(8,0) + Cl(8,0): a 512-float block [u | v]
+// (x = u + v e8) is the pair (u + v w, u - v w), w = e0 ... e7, multiplied
+// componentwise; back, u = (P + Q)/2 and v = (P - Q) w / 2, which is also the
+// adjoint map for the backward sums. Used by the Cl(9,0,1) product (pga10.cu).
+__device__ __forceinline__ float wsign9(uint32_t j) { return (__popc(j & 0xAAu) & 1) ? -1.0f : 1.0f; }
+__device__ __forceinline__ float gsign9(uint32_t j) { return (__popc(j) & 1) ? -1.0f : 1.0f; }
+
+// As gather, for component cs (+1 / -1) of the block [u | v] (optionally of
+// its grade involution, folded into S and C by the caller):
+//   row[idx] = u[idx] + sign_K * C * v[255 - idx]
+// with the compile-time part of w(255 - idx) in sign_K and its lane part,
+// the component sign and the involution's v sign in C (C0 / C3 for the two
+// lane codes q, q ^ 3).
+template <int K>
+__device__ __forceinline__ void gather9_1(float (&r)[64], const float *u, const float *v, int qx0,
+                                          int qx3, const float (&S)[4], float C0, float C3) {
+    constexpr int m = popc8(K);
+    constexpr int wk = popc8((~K) & 0x2A) & 1;  // bits 3, 5, 7 of ~(4K + q')
+    const int idx = 4 * K + ((m & 1) ? qx3 : qx0);
+    const float c = ((m & 1) ? C3 : C0) * (wk ? -1.0f : 1.0f);
+    const float val = fmaf(c, v[255 - idx], u[idx]) * S[m & 3];
+    r[slot_of(K)] = sig1_of(K) > 0 ? val : -val;
+}
+template <int... K>
+__device__ __forceinline__ void gather9(float (&r)[64], const float *u, const float *v, int q,
+                                        const float (&S)[4], float C0, float C3,
+                                        std::integer_sequence<int, K...>) {
+    (gather9_1<K>(r, u, v, q, q ^ 3, S, C0, C3), ...);
+}
+
+struct Gp9Args {
+    const float *x, *y;  // rows of 1024 floats; blocks hx, hy
+    float *out;          // block ho of rows of 1024 floats
+    int hx, hy, ho;
+    int gx, gy;          // use the grade involution of the x / y block
+    int gout, acc;       // grade involution of the result; add into out
+};
+
+// out_block (+)= g?(sum of mode MODE over Cl(9,0) blocks), 4 rows per warp
+// and batch: product slot p = 2 * row + component; u of a block is loaded
+// into the slot of component +, v into that of component -.
+template <int MODE>
+__global__ void __launch_bounds__(32)
+    gp9_kernel(Gp9Args A, int64_t batch, int64_t nbatches, int *err) {
+    constexpr bool SWAP = MODE == CB_MODE_GRAD_A;
+    constexpr bool TU = MODE == CB_MODE_GRAD_B, TV = MODE == CB_MODE_GRAD_A;
+    const float *gu = SWAP ? A.y : A.x, *gv = SWAP ? A.x : A.y;
+    const int hu = SWAP ? A.hy : A.hx, hv = SWAP ? A.hx : A.hy;
+    const bool giu = SWAP ? A.gy : A.gx, giv = SWAP ? A.gx : A.gy;
+    extern __shared__ __align__(16) float sm[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + kBufFloats);
+    const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
+    const int r4 = q >> 1, c4 = r4 ^ (q & 1);
+    const int prow = p >> 1;                         // row of this slot in the batch
+    const float cs = (p & 1) ? -1.0f : 1.0f;         // component
+    if (lane == 0) {
+        mbar_init(full, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    // Lane factors (see gp_mat16_kernel), per operand with the grade
+    // involution folded in: it multiplies u[idx] by (-1)^popc(idx), whose
+    // parity is popc(K) + popc(q), and turns v into -g(v), i.e. flips C.
+    float s_u[4], s_v[4], s_out[4];
+    const int qpar = (q ^ (q >> 1)) & 1;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const float s = (float)last_sign(q, m);
+        const float sl = q == 2 ? -s : s;
+        const float gi = ((m & 1) ^ qpar) ? -1.0f : 1.0f;
+        s_u[m] = giu ? sl * gi : sl;
+        s_v[m] = giv ? sl * gi : sl;
+        s_out[m] = sl * 0.0625f;
+    }
+    // lane part of w(~idx): bit 1 of ~q' (q' = q, or q ^ 3 for odd K)
+    const float w0 = ((q >> 1) & 1) ? 1.0f : -1.0f, w3 = ((q >> 1) & 1) ? -1.0f : 1.0f;
+    const float cu = giu ? -cs : cs, cv = giv ? -cs : cs;
+    const float c_fwd = r4 ? 1.0f : -1.0f;
+    const float c_inv = r4 ? -1.0f : 1.0f;
+    bool ok = true;
+    int64_t bt = blockIdx.x;
+    for (int it = 0; bt < nbatches && ok; bt += gridDim.x, ++it) {
+        const int64_t r0 = bt * 4;
+        const int nv = (int)std::min<int64_t>(4, batch - r0);
+        if (lane == 0) {
+            bulk_wait_read<0>();  // the previous batch's stores have read the buffer
+            mbar_arrive_expect_tx(full, (uint32_t)nv * 4096u);
+            for (int i = 0; i < nv; ++i) {
+                const float *xu = gu + (r0 + i) * 1024 + hu * 512;
+                const float *yu = gv + (r0 + i) * 1024 + hv * 512;
+                bulk_load(sm + (2 * i) * kRowFloats, xu, 1024, full);
+                bulk_load(sm + (2 * i + 1) * kRowFloats, xu + 256, 1024, full);
+                bulk_load(sm + kRegion + (2 * i) * kRowFloats, yu, 1024, full);
+                bulk_load(sm + kRegion + (2 * i + 1) * kRowFloats, yu + 256, 1024, full);
+            }
+        }
+        ok = mbar_wait_bounded(full, it & 1, err, 0x311);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        float *U = sm + p * kRowFloats;
+        float *V = U + kRegion;
+        float r[64];
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) {
+            const float *raw = sm + (t == 0 ? 0 : kRegion) + (2 * prow) * kRowFloats;
+            const float c = t == 0 ? cu : cv;
+            gather9(r, raw, raw + kRowFloats, q, t == 0 ? s_u : s_v, c * w0, c * w3,
+                    std::make_integer_sequence<int, 64>{});
+            __syncwarp();  // both components of the row have read the raw block
+            to_matrix3(r);
+            factor4(r, c_fwd);
+            const bool trans = t == 0 ? TU : TV;
+            store_quadrant_rt(t == 0 ? U : V, trans ? c4 * 2 + r4 : r4 * 2 + c4, t == 0 ? !TU : TV,
+                              r);
+        }
+        __syncwarp();
+        quadrant_product(r, U, V, r4, c4);
+        __syncwarp();
+        factor4(r, c_inv);
+        from_matrix3(r);
+        scatter(r, U, q, s_out, std::make_integer_sequence<int, 64>{});
+        __syncwarp();
+        // merge: slot 2r holds P (component +), slot 2r + 1 holds Q; lanes 8r..8r+7
+        // take the blade pairs (k, ~k), so every lane reads and writes its own places
+        const int mrow = lane >> 3, j8 = lane & 7;
+        if (mrow < nv) {
+            float *Pz = sm + (2 * mrow) * kRowFloats, *Qz = Pz + kRowFloats;
+            const float *old = A.out + (r0 + mrow) * 1024 + A.ho * 512;
+#pragma unroll 4
+            for (int t = 0; t < 16; ++t) {
+                const uint32_t k = j8 + 8 * t, nk = 255 - k;
+                const float P = Pz[k], Q = Qz[k], Pr = Pz[nk], Qr = Qz[nk];
+                float uk = 0.5f * (P + Q), unk = 0.5f * (Pr + Qr);
+                float vk = 0.5f * wsign9(nk) * (Pr - Qr), vnk = 0.5f * wsign9(k) * (P - Q);
+                if (A.gout) {  // g(u + v e8) = g(u) - g(v) e8
+                    const float gk = gsign9(k), gnk = gsign9(nk);
+                    uk *= gk; unk *= gnk; vk *= -gk; vnk *= -gnk;
+                }
+                if (A.acc) {
+                    uk += old[k]; unk += old[nk]; vk += old[256 + k]; vnk += old[256 + nk];
+                }
+                Pz[k] = uk; Pz[nk] = unk; Qz[k] = vk; Qz[nk] = vnk;
+            }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            for (int i = 0; i < nv; ++i) {
+                float *o = A.out + (r0 + i) * 1024 + A.ho * 512;
+                bulk_store(o, sm + (2 * i) * kRowFloats, 1024);
+                bulk_store(o + 256, sm + (2 * i + 1) * kRowFloats, 1024);
+            }
+            bulk_commit();
+        }
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+template <int MODE>
+int launch_gp9(const Gp9Args &A, int64_t batch, cudaStream_t s) {
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    int *err = nullptr;
+    if ((st = device_error_word(&err))) return st;
+    auto kern = gp9_kernel<MODE>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gp9)");
+    int ps = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, kern, 32, kSmemBytes) != cudaSuccess ||
+        ps < 1) {
+        cudaGetLastError();
+        ps = 1;
+    }
+    const int64_t nb = (batch + 3) / 4;
+    const int grid = (int)std::min<int64_t>(nb, (int64_t)ps * di.sm_count);
+    kern<<<grid, 32, kSmemBytes, s>>>(A, batch, nb, err);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp9_kernel");
+}
+
 // Both backward sums in one pass over a, b, g (5 KB per product instead of 6 KB
 // for two launches), in two phases that run the same code:
 //   phase 0: a and g load; rho(a)^T (the A operand) and rho(g) (the B
@@ -743,6 +924,18 @@ int gp_layer_weight(const float *w, float *mats, cudaStream_t s) {
     gp_layer_weight_kernel<<<1, 32, 0, s>>>(w, mats);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_layer_weight_kernel");
+}
+
+// One Cl(9,0) sum of blocks (see gp9_kernel); mode as in cb_bilinear.
+int gp9(int mode, const float *x, int hx, int gx, const float *y, int hy, int gy, float *out,
+        int ho, int gout, int acc, int64_t batch, cudaStream_t s) {
+    if (batch == 0) return CB_OK;
+    const Gp9Args A{x, y, out, hx, hy, ho, gx, gy, gout, acc};
+    switch (mode) {
+    case CB_MODE_FWD: return launch_gp9<CB_MODE_FWD>(A, batch, s);
+    case CB_MODE_GRAD_A: return launch_gp9<CB_MODE_GRAD_A>(A, batch, s);
+    default: return launch_gp9<CB_MODE_GRAD_B>(A, batch, s);
+    }
 }
 
 }  // namespace cb

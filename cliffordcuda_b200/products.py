@@ -16,8 +16,6 @@ metric travels as two bitmasks. Backward sums (reference
 """
 from __future__ import annotations
 
-import ctypes
-
 import torch
 
 from . import _lib
@@ -63,22 +61,6 @@ def _dims(a, b):
     return n
 
 
-def _aligned(*ts):
-    return all(t is None or t.data_ptr() % 16 == 0 for t in ts)
-
-
-def _workspace(op, n, neg, zero, batch, device):
-    """Caller workspace for the routes that need one (cb_bilinear_workspace_bytes),
-    or None when the request takes none."""
-    wb = ctypes.c_int64()
-    _lib.check(_lib.load().cb_bilinear_workspace_bytes(_lib.OPS[op], n, neg, zero, batch,
-                                                       ctypes.byref(wb)),
-               "cb_bilinear_workspace_bytes")
-    if wb.value == 0:
-        return None
-    return torch.empty(wb.value, device=device, dtype=torch.uint8)
-
-
 def bilinear_raw(op, mode, x, y, n, metric, out=None, direct=False):
     """One native bilinear sum (no autograd). x, y contiguous fp32 CUDA.
     direct=True always uses the blade-by-blade kernels (cb_bilinear_direct)."""
@@ -86,15 +68,6 @@ def bilinear_raw(op, mode, x, y, n, metric, out=None, direct=False):
     if out is None:
         out = torch.empty_like(x)
     lib = _lib.load()
-    ws = None if direct or mode != "fwd" or not _aligned(x, y, out) else \
-        _workspace(op, n, neg, zero, x.shape[0], x.device)
-    if ws is not None:
-        with torch.cuda.device(x.device):
-            st = lib.cb_bilinear_ws(_lib.OPS[op], _lib.MODES[mode], _lib.ptr(x), _lib.ptr(y),
-                                    _lib.ptr(out), x.shape[0], n, neg, zero, _lib.ptr(ws),
-                                    ws.numel(), _lib.stream_of(x))
-        _lib.check(st, f"cb_bilinear_ws({op}, {mode})")
-        return out
     fn = lib.cb_bilinear_direct if direct else lib.cb_bilinear
     with torch.cuda.device(x.device):
         st = fn(_lib.OPS[op], _lib.MODES[mode], _lib.ptr(x), _lib.ptr(y),
@@ -108,14 +81,6 @@ def bilinear_bwd_raw(op, a, b, g, n, metric, ga=None, gb=None):
     may be None to skip it. a, b, g contiguous fp32 CUDA."""
     neg, zero = metric_masks(metric)
     lib = _lib.load()
-    ws = _workspace(op, n, neg, zero, a.shape[0], g.device) if _aligned(a, b, g, ga, gb) else None
-    if ws is not None:
-        with torch.cuda.device(g.device):
-            st = lib.cb_bilinear_bwd_ws(_lib.OPS[op], _lib.ptr(a), _lib.ptr(b), _lib.ptr(g),
-                                        _lib.ptr(ga), _lib.ptr(gb), a.shape[0], n, neg, zero,
-                                        _lib.ptr(ws), ws.numel(), _lib.stream_of(g))
-        _lib.check(st, f"cb_bilinear_bwd_ws({op})")
-        return ga, gb
     with torch.cuda.device(g.device):
         st = lib.cb_bilinear_bwd(_lib.OPS[op], _lib.ptr(a), _lib.ptr(b), _lib.ptr(g),
                                  _lib.ptr(ga), _lib.ptr(gb), a.shape[0], n, neg, zero,

@@ -71,8 +71,10 @@ CB_API int cb_bilinear(int op, int mode, const float *x, const float *y, float *
 /*
  * As cb_bilinear, always through the blade-by-blade sum kernels: the sum
  * out[i ^ j] += s(i, j) x_i y_j evaluated term by term on the CUDA cores.
- * cb_bilinear takes a faster route for the Euclidean Cl(8,0) geometric
- * product (its real 16 x 16 matrix representation; same results to fp32
+ * cb_bilinear takes faster routes for two geometric products: Euclidean
+ * Cl(8,0) through its real 16 x 16 matrix representation, and Cl(9,0,1)
+ * (e0..e8 square to +1, e9 to 0) as dual numbers over Cl(9,0) =
+ * Cl(8,0) + Cl(8,0), six 16 x 16 products per sum (same results to fp32
  * rounding); this entry point keeps the term-by-term kernels reachable, for
  * comparison and for callers that want them. Same reference interface as
  * cb_bilinear (extensions/ga/geom_prod.py:216-250 and its siblings).
@@ -91,27 +93,6 @@ CB_API int cb_bilinear_direct(int op, int mode, const float *x, const float *y, 
 CB_API int cb_bilinear_bwd(int op, const float *a, const float *b, const float *g,
                            float *grad_a, float *grad_b, int64_t batch, int n,
                            uint32_t neg_mask, uint32_t zero_mask, void *stream);
-
-/*
- * The same sums with a caller workspace, which lets the library take routes
- * that keep intermediates in device memory. Today one route uses it: the
- * geometric product of Cl(9,0,1) (n = 10, e0..e8 squaring to +1, e9 to 0),
- * computed through six Cl(8,0) matrix-representation products per sum
- * instead of the 4^10-term direct sum (same results to fp32 rounding). For
- * every other request the workspace is unused (0 bytes) and the calls behave
- * as cb_bilinear / cb_bilinear_bwd. Same reference interface as those
- * (extensions/ga/geom_prod.py:216-276; the reference always ran its direct
- * LUT kernel). The route needs 16-byte aligned rows and workspace.
- */
-CB_API int cb_bilinear_workspace_bytes(int op, int n, uint32_t neg_mask, uint32_t zero_mask,
-                                       int64_t batch, int64_t *bytes);
-CB_API int cb_bilinear_ws(int op, int mode, const float *x, const float *y, float *out,
-                          int64_t batch, int n, uint32_t neg_mask, uint32_t zero_mask,
-                          void *workspace, int64_t workspace_bytes, void *stream);
-CB_API int cb_bilinear_bwd_ws(int op, const float *a, const float *b, const float *g,
-                              float *grad_a, float *grad_b, int64_t batch, int n,
-                              uint32_t neg_mask, uint32_t zero_mask, void *workspace,
-                              int64_t workspace_bytes, void *stream);
 
 /* -------------------------------------------------------- blade maps --
  * One-pass per-blade maps of CliffordAlgebra on (batch, 2^n) rows, 1 <= n <= 24.

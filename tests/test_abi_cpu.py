@@ -98,14 +98,3 @@ def test_blade_map_arguments_rejected():
     assert lib.cb_norm_sq(p, q, 4, 0, 0, 0, NULL) == 3               # n = 0
     assert lib.cb_norm_sq(p, q, 4, 5, 1, 1, NULL) == 1               # both masks
 
-
-def test_workspace_query():
-    """cb_bilinear_workspace_bytes: the Cl(9,0,1) geometric product takes a
-    workspace (its Cl(8,0) planes); every other request takes none."""
-    lib = _lib.load()
-    b = ctypes.c_int64()
-    assert lib.cb_bilinear_workspace_bytes(0, 10, 0, 1 << 9, 100, ctypes.byref(b)) == 0
-    assert b.value == 26 * 100 * 1024
-    for op, n, neg, zero in ((3, 10, 0, 1 << 9), (0, 10, 1, 1 << 9), (0, 8, 0, 0)):
-        assert lib.cb_bilinear_workspace_bytes(op, n, neg, zero, 100, ctypes.byref(b)) == 0
-        assert b.value == 0
