@@ -203,8 +203,8 @@ def main():
     ap.add_argument("--config-steps", type=int, default=10,
                     help="timed steps of each config measurement in the default run")
     ap.add_argument("--workload", default="headline",
-                    choices=["headline", "products", "layer", "rotor", "pga"],
-                    help="headline = the BASELINE metric; the others measure configs 2-5")
+                    choices=["headline", "products", "layer", "rotor", "pga", "large"],
+                    help="headline = the BASELINE metric; products|layer|rotor|pga measure configs 2-5, large the n = 12..16 regime")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -328,7 +328,39 @@ def pga(args, world, rank, dev, T):
                  "products/s", total, clk, cfg, {"ops": res})
 
 
-WORKLOADS = {"products": products, "layer": layer, "rotor": rotor, "pga": pga}
+def large(args, world, rank, dev, T):
+    """Large algebras (not a BASELINE config; the reference's own large-n tests
+    use these signatures): the geometric product fwd + both grads at n = 12, 14
+    and 16 on the wide kernel, against the FP32 peak (2 * 4^n flops per sum)."""
+    from cliffordcuda_b200.products import bilinear_bwd_raw, bilinear_raw
+    res = {}
+    total = 0.0
+    clk = None
+    for n, metric, B0 in ((12, (1,) * 12, 2048), (14, (1,) * 12 + (-1, -1), 128),
+                          (16, (1,) * 13 + (-1, -1, 0), 8)):
+        D = 1 << n
+        B = args.batch or max(1, B0 // world)
+        gen = torch.Generator(device=dev).manual_seed(n + rank)
+        a, b, g = (torch.randn(B, D, device=dev, generator=gen) for _ in range(3))
+        outs = [torch.empty_like(a) for _ in range(3)]
+
+        def step():
+            bilinear_raw("gp", "fwd", a, b, n, metric, out=outs[0])
+            bilinear_bwd_raw("gp", a, b, g, n, metric, outs[1], outs[2])
+        ms, clk = T.time(step, args.steps, args.warmup)
+        total += ms
+        flops = 3 * 2 * (4 ** n) * B
+        res[f"n{n}"] = {"metric": list(metric), "batch": B, "products_per_s": world * B / (ms / 1e3),
+                        "ms_per_step": ms, "pct_fp32_peak":
+                            100 * flops / (ms / 1e3) / 1e12 / fp32_peak_tflops(dev)}
+        del a, b, g, outs
+    cfg = {"workload": "geometric product fwd+bwd at n = 12, 14, 16 (wide kernel)",
+           "l2": "n = 12: inputs 100 MB; n = 14, 16: compute-bound"}
+    return _line(args, world, "large-n gp fwd+bwd, % of FP32 peak", res["n14"]["pct_fp32_peak"],
+                 "% FP32 peak", total, clk, cfg, {"sizes": res})
+
+
+WORKLOADS = {"products": products, "layer": layer, "rotor": rotor, "pga": pga, "large": large}
 
 
 def collect(args, world, rank, dev):
