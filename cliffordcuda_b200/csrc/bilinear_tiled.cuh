@@ -47,7 +47,10 @@
 // P == Q terms.
 #pragma once
 #include <algorithm>
+#include <map>
+#include <mutex>
 #include <cstdio>
+#include <type_traits>
 #include <utility>
 
 #include "common.cuh"
@@ -264,7 +267,7 @@ __device__ __forceinline__ void apply_sign(float (&yv)[kBlk], float2 sg) {
 // of the high parts times the high-part predicate (.x, for even-parity y
 // elements); .y adds the y side of the cross term for odd-parity y elements:
 // (-1)^popc(i_h) for the forward sum and grad_b, (-1)^popc(k_h) for grad_a.
-__device__ __forceinline__ float2 high_factor(int mode, int opk, uint32_t ih, uint32_t kh,
+__host__ __device__ __forceinline__ float2 high_factor(int mode, int opk, uint32_t ih, uint32_t kh,
                                               uint32_t negH, uint32_t zeroH) {
     const uint32_t jh = ih ^ kh;
     const uint32_t P = (mode == CB_MODE_GRAD_A) ? kh : ih;
@@ -283,9 +286,199 @@ __host__ __device__ inline size_t table_entries(int n, bool inner) {
     return nh * nh * (inner ? 2 : 1);
 }
 
-__host__ __device__ inline size_t smem_bytes(int n, bool inner) {
+// Balanced step schedule of the sparse products (wedge, contractions,
+// regressive). Output block k_h has cnt(k_h) steps with a non-zero high-part
+// factor, and these counts differ widely (for the left contraction's forward
+// sum, 2^(#high generators not in k_h)): a lane that owns block k_h alone
+// runs cnt(k_h) steps while its warp waits for the largest count. The
+// schedule moves the tail of each heavy block's step list to lanes whose own
+// list is short. Such a lane runs its borrowed segment first, parks that sum
+// in a second accumulator, then runs its own steps; after the sweep the
+// parked sums pass through the row's (then dead) y lines to the owning lane,
+// which adds them in ascending donor order, so results stay deterministic.
+// A lane borrows at most one segment. Steps per lane: ih[t * NH + lane],
+// t < ntot[lane], the first nsec[lane] of them for block sec_kh[lane].
+constexpr int kMaxNH = 32;
+struct StepSched {
+    unsigned char ih[kMaxNH * kMaxNH];
+    unsigned char nsec[kMaxNH], ntot[kMaxNH], sec_kh[kMaxNH], pad_[kMaxNH];
+    uint32_t donors[kMaxNH];  // lanes whose borrowed segment is for this block
+    int T;                    // steps of the longest lane; 0: dense sweep
+    int pad2_[3];
+};
+
+// Shared-memory bank conflicts of a round: the eight lanes of a quarter-warp
+// read eight lines at once, and lines whose indices agree in the low three
+// bits (the swizzle phase) but differ collide unless they are the same line.
+inline int round_conflicts(const int *lines, int nl) {
+    int cost = 0;
+    for (int q0 = 0; q0 < nl; q0 += 8) {
+        for (int ph = 0; ph < 8; ++ph) {
+            int distinct[8], nd = 0;
+            for (int l = q0; l < q0 + 8 && l < nl; ++l) {
+                if (lines[l] < 0 || (lines[l] & 7) != ph) continue;
+                bool seen = false;
+                for (int d = 0; d < nd; ++d) seen |= distinct[d] == lines[l];
+                if (!seen) distinct[nd++] = lines[l];
+            }
+            if (nd > 1) cost += nd - 1;
+        }
+    }
+    return cost;
+}
+
+// Reorders each lane's steps within its borrowed and its own segment (the
+// sums do not depend on the order beyond rounding) so that the lanes of a
+// round read x lines (i_h) and y lines (i_h ^ k_h) with few bank conflicts:
+// greedy, round by round.
+inline void order_steps(StepSched &t, int NH) {
+    unsigned char out[kMaxNH * kMaxNH];
+    bool used[kMaxNH][kMaxNH] = {};
+    for (int r = 0; r < t.T; ++r) {
+        int xl[kMaxNH], yl[kMaxNH];
+        for (int L = 0; L < NH; ++L) xl[L] = yl[L] = -1;
+        for (int L = 0; L < NH; ++L) {
+            if (r >= t.ntot[L]) continue;
+            const bool sec = r < t.nsec[L];
+            const int lo = sec ? 0 : t.nsec[L], hi = sec ? t.nsec[L] : t.ntot[L];
+            const int k = sec ? t.sec_kh[L] : L;
+            int best = -1, best_cost = 1 << 30;
+            for (int c = lo; c < hi; ++c) {
+                if (used[L][c]) continue;
+                const int ih = t.ih[c * NH + L];
+                xl[L] = ih;
+                yl[L] = ih ^ k;
+                const int cost = round_conflicts(xl, L + 1) + round_conflicts(yl, L + 1);
+                if (cost < best_cost) {
+                    best_cost = cost;
+                    best = c;
+                }
+            }
+            used[L][best] = true;
+            const int ih = t.ih[best * NH + L];
+            xl[L] = ih;
+            yl[L] = ih ^ k;
+            out[r * NH + L] = (unsigned char)ih;
+        }
+    }
+    for (int L = 0; L < NH; ++L)
+        for (int r = 0; r < t.ntot[L]; ++r) t.ih[r * NH + L] = out[r * NH + L];
+    // then swaps of two steps of one lane's segment while they lower the
+    // conflicts of the two rounds involved
+    auto cost_of = [&](int r) {
+        int xl[kMaxNH], yl[kMaxNH];
+        for (int L = 0; L < NH; ++L) {
+            xl[L] = yl[L] = -1;
+            if (r < t.ntot[L]) {
+                xl[L] = t.ih[r * NH + L];
+                yl[L] = xl[L] ^ (r < t.nsec[L] ? t.sec_kh[L] : L);
+            }
+        }
+        return round_conflicts(xl, NH) + round_conflicts(yl, NH);
+    };
+    for (int pass = 0; pass < 8; ++pass) {
+        bool improved = false;
+        for (int L = 0; L < NH; ++L)
+            for (int r1 = 0; r1 < t.ntot[L]; ++r1)
+                for (int r2 = r1 + 1; r2 < t.ntot[L]; ++r2) {
+                    if ((r1 < t.nsec[L]) != (r2 < t.nsec[L])) continue;
+                    const int before = cost_of(r1) + cost_of(r2);
+                    std::swap(t.ih[r1 * NH + L], t.ih[r2 * NH + L]);
+                    if (cost_of(r1) + cost_of(r2) < before) {
+                        improved = true;
+                    } else {
+                        std::swap(t.ih[r1 * NH + L], t.ih[r2 * NH + L]);
+                    }
+                }
+        if (!improved) break;
+    }
+}
+
+// Builds the schedule for one sum; inactive (T = 0) unless it cuts the
+// longest lane's steps by 1.5x or more: the scheduled sweep reads x lines that
+// differ across lanes (no broadcast) and parks a second sum, which costs more
+// than it saves where the sum is bound by HBM (the sparse products at n <= 7).
+inline StepSched make_sched(int mode, int opk, int n, uint32_t neg, uint32_t zero) {
+    StepSched s{};
+    if (opk == OPK_GP || opk == OPK_INNER) return s;
+    const int opb = opk == OPK_REG ? OPK_WEDGE : opk;
+    const int lgNH = n - kLow, NH = 1 << lgNH;
+    const uint32_t negH = neg >> kLow, zeroH = zero >> kLow;
+    unsigned char list[kMaxNH][kMaxNH];
+    int cnt[kMaxNH] = {}, total = 0, maxc = 0;
+    for (int k = 0; k < NH; ++k) {
+        for (int ih = 0; ih < NH; ++ih)
+            if (high_factor(mode, opb, ih, k, negH, zeroH).x != 0.0f) list[k][cnt[k]++] = ih;
+        total += cnt[k];
+        maxc = std::max(maxc, cnt[k]);
+    }
+    for (int T = (total + NH - 1) / NH; 3 * T <= 2 * maxc; ++T) {
+        int keep[kMaxNH], cap[kMaxNH], order[kMaxNH];
+        for (int k = 0; k < NH; ++k) {
+            keep[k] = std::min(cnt[k], T);
+            cap[k] = std::max(0, T - cnt[k]);
+            order[k] = k;
+        }
+        // heavy blocks by excess and donors by spare capacity, largest first
+        std::sort(order, order + NH, [&](int a, int b) {
+            return cnt[a] != cnt[b] ? cnt[a] > cnt[b] : a < b;
+        });
+        StepSched t{};
+        int next_donor = NH - 1;  // order[] from the end: the lightest lanes
+        bool ok = true;
+        for (int h = 0; h < NH && ok; ++h) {
+            const int k = order[h];
+            int pos = keep[k];
+            while (pos < cnt[k]) {
+                while (next_donor >= 0 && cap[order[next_donor]] == 0) --next_donor;
+                if (next_donor < 0) {
+                    ok = false;
+                    break;
+                }
+                const int d = order[next_donor--];
+                const int seg = std::min(cap[d], cnt[k] - pos);
+                t.sec_kh[d] = (unsigned char)k;
+                t.nsec[d] = (unsigned char)seg;
+                for (int q = 0; q < seg; ++q) t.ih[q * NH + d] = list[k][pos + q];
+                t.donors[k] |= 1u << d;
+                pos += seg;
+            }
+        }
+        if (!ok) continue;
+        for (int k = 0; k < NH; ++k) {
+            for (int q = 0; q < keep[k]; ++q) t.ih[(t.nsec[k] + q) * NH + k] = list[k][q];
+            t.ntot[k] = (unsigned char)(t.nsec[k] + keep[k]);
+        }
+        t.T = T;
+        order_steps(t, NH);
+        return t;
+    }
+    return s;
+}
+
+// The schedule for one sum, built once per (sum, product, n, metric).
+inline StepSched cached_sched(int mode, int opk, int n, uint32_t neg, uint32_t zero) {
+    static std::mutex mu;
+    static std::map<uint64_t, StepSched> cache;
+    const uint64_t key = ((uint64_t)neg << 32) ^ ((uint64_t)zero << 12) ^ (uint64_t)(mode << 8) ^
+                         (uint64_t)(opk << 4) ^ (uint64_t)n;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    const StepSched s = make_sched(mode, opk, n, neg, zero);
+    cache.emplace(key, s);
+    return s;
+}
+
+// The dense sweep's kernels take this in place of a StepSched (no parameter
+// space or shared memory spent on a schedule they do not use).
+struct NoSched {
+    int T;
+};
+
+__host__ __device__ inline size_t smem_bytes(int n, bool inner, bool sched = false) {
     return 1024 /* alignment slack */ + 2 * kStages * size_t(kTileBytes) +
-           table_entries(n, inner) * sizeof(float2) + 64;
+           table_entries(n, inner) * sizeof(float2) + 64 + (sched ? sizeof(StepSched) : 0);
 }
 
 template <int MODE, int OPK, int NEGL>
@@ -330,6 +523,47 @@ __device__ __forceinline__ void sweep(float (&acc)[kBlk], const float *xt, const
     }
 }
 
+// The sweep under a StepSched (single-product bodies only): this lane's
+// borrowed steps into acc, parked in acc2, then its own steps into acc.
+template <int MODE, int OPK, int NEGL>
+__device__ __forceinline__ void sweep_sched(float (&acc)[kBlk], float (&acc2)[kBlk],
+                                            const float *xt, const float *yt, const float2 *tab,
+                                            int rowl, int kh, int lgNH, const unsigned char *steps,
+                                            int nsec, int ntot, int skh) {
+    const int NH = 1 << lgNH;
+#pragma unroll 1
+    for (int t = 0; t < ntot; ++t) {
+        if (t == nsec && nsec > 0) {
+#pragma unroll
+            for (int e = 0; e < kBlk; ++e) {
+                acc2[e] = acc[e];
+                acc[e] = 0.0f;
+            }
+        }
+        const int k = t < nsec ? skh : kh;
+        const int ih = steps[t * NH + kh];
+        const float2 sg = tab[(ih << lgNH) | k];
+        float xv[kBlk], yv[kBlk];
+        load_block(xt, rowl + ih, xv);
+        load_block(yt, rowl + (ih ^ k), yv);
+        if (MODE == CB_MODE_GRAD_B) {
+            const float sx = parity(ih) ? -1.0f : 1.0f;
+#pragma unroll
+            for (int e = 0; e < kBlk; ++e)
+                if (popcl(e) & 1) xv[e] *= sx;
+        }
+        apply_sign(yv, sg);
+        block_fma<MODE, OPK, NEGL>(acc, xv, yv);
+    }
+    if (nsec > 0 && ntot == nsec) {
+#pragma unroll
+        for (int e = 0; e < kBlk; ++e) {
+            acc2[e] = acc[e];
+            acc[e] = 0.0f;
+        }
+    }
+}
+
 // Sign s_L(e, e) (-1)^(popc(k_h) popc(e)) of the diagonal term e of line k_h
 // (the inner product's correction).
 template <int NEGL>
@@ -338,13 +572,14 @@ __device__ __forceinline__ int diag_sign(int e, int kh) {
                ? -1 : 1;
 }
 
-template <int MODE, int OPK, int NEGL>
+template <int MODE, int OPK, int NEGL, bool SCHED>
 __global__ void __launch_bounds__(kThreads, 3)
     bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
                           const __grid_constant__ CUtensorMap my,
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
                           uint32_t zero, int num_tiles, int *err, bool skip_zero,
-                          const LowRelabel rl) {
+                          const LowRelabel rl,
+                          const __grid_constant__ std::conditional_t<SCHED, StepSched, NoSched> sched) {
     extern __shared__ unsigned char smem_raw[];
     // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
@@ -361,6 +596,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     uint64_t *bars = reinterpret_cast<uint64_t *>(tab + table_entries(n, inner));
     uint64_t *full = bars;
     int *done_count = reinterpret_cast<int *>(bars + kStages);  // [kStages]
+    StepSched *sch = reinterpret_cast<StepSched *>(bars + 8);   // 64 bytes past the barriers
+    constexpr bool scheduled = SCHED && !inner && OPK != OPK_GP;  // sched.T > 0
 
     const int tid = threadIdx.x;
     const int D = 1 << n;
@@ -375,6 +612,11 @@ __global__ void __launch_bounds__(kThreads, 3)
         prefetch_tensormap(&mx);
         prefetch_tensormap(&my);
         prefetch_tensormap(&mo);
+    }
+    if constexpr (scheduled) {  // lanes index the schedule by lane: shared, not the constant bank
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&sched);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(sch);
+        for (int w = tid; w < (int)(sizeof(StepSched) / 4); w += kThreads) dst[w] = src[w];
     }
     // per-CTA table of high-part factors, [i_h][k_h]
     for (int e = tid; e < NH * NH; e += kThreads) {
@@ -434,7 +676,27 @@ __global__ void __launch_bounds__(kThreads, 3)
         float acc[kBlk];
 #pragma unroll
         for (int e = 0; e < kBlk; ++e) acc[e] = 0.0f;
-        sweep<MODE, OPB, NEGL>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
+        if constexpr (scheduled) {
+            {
+                float acc2[kBlk];
+                const int nsec = sch->nsec[kh];
+                sweep_sched<MODE, OPB, NEGL>(acc, acc2, xt, yt, tab, rowl, kh, lgNH, sch->ih, nsec,
+                                             sch->ntot[kh], sch->sec_kh[kh]);
+                // every lane of the row is past its sweep: the row's y lines are
+                // free to carry the borrowed sums to their blocks' lanes
+                __syncwarp();
+                if (nsec > 0) store_block(yt, rowl + kh, acc2);
+                __syncwarp();
+                for (uint32_t dm = sch->donors[kh]; dm; dm &= dm - 1) {
+                    float part[kBlk];
+                    load_block(yt, rowl + __ffs(dm) - 1, part);
+#pragma unroll
+                    for (int e = 0; e < kBlk; ++e) acc[e] += part[e];
+                }
+            }
+        } else {
+            sweep<MODE, OPB, NEGL>(acc, xt, yt, tab, tab2, rowl, kh, lgNH, skip_zero);
+        }
 
         if (MODE == CB_MODE_GRAD_A && parity(kh)) {
 #pragma unroll
@@ -512,31 +774,39 @@ int launch_tiled_k(const float *x, const float *y, float *out, int64_t batch, in
     if ((st = make_tmap_lines(&mx, x, lines, kTileLines))) return st;
     if ((st = make_tmap_lines(&my, y, lines, kTileLines))) return st;
     if ((st = make_tmap_lines(&mo, out, lines, kTileLines))) return st;
-    const size_t smem = smem_bytes(n, OPK == OPK_INNER);
-    auto kern = bilinear_tiled_kernel<MODE, OPK, NEGL>;
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bilinear_tiled)");
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    if (per_sm < 1) {
-        set_error("bilinear tiled kernel does not fit an SM (smem %zu)", smem);
-        return CB_ERR_UNSUPPORTED;
-    }
     const int rows_per_tile = kTileFloats / D;
     const int64_t tiles = (batch + rows_per_tile - 1) / rows_per_tile;
     if (tiles > ((int64_t)1 << 30)) {
         set_error("batch too large for one call");
         return CB_ERR_UNSUPPORTED;
     }
-    const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * di.sm_count);
     const bool skip_zero = n >= 9 || (zero >> kLow) != 0;
-    kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err, skip_zero,
-                                           rl);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "launch bilinear_tiled_kernel");
-    return CB_OK;
+    auto run = [&](auto kern, size_t smem, const auto &sched_arg) -> int {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(bilinear_tiled)");
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (per_sm < 1) {
+            set_error("bilinear tiled kernel does not fit an SM (smem %zu)", smem);
+            return CB_ERR_UNSUPPORTED;
+        }
+        const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * di.sm_count);
+        kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err,
+                                               skip_zero, rl, sched_arg);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "launch bilinear_tiled_kernel");
+        return CB_OK;
+    };
+    if constexpr (OPK != OPK_GP && OPK != OPK_INNER) {
+        const StepSched sched = cached_sched(MODE, OPK, n, neg, zero);
+        if (sched.T)
+            return run(bilinear_tiled_kernel<MODE, OPK, NEGL, true>, smem_bytes(n, false, true),
+                       sched);
+    }
+    return run(bilinear_tiled_kernel<MODE, OPK, NEGL, false>, smem_bytes(n, OPK == OPK_INNER),
+               NoSched{0});
 }
 
 // Low generators squaring to -1 are relabelled to the top of the low block
