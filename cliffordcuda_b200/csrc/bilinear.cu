@@ -12,6 +12,9 @@ template <int MODE>
 int bilinear_tiled(int op, const float *x, const float *y, float *out, int64_t batch, int n,
                    uint32_t neg, uint32_t zero, cudaStream_t stream);
 template <int MODE>
+int bilinear_tiled_cl61(const float *x, const float *y, float *out, int64_t batch,
+                        cudaStream_t stream);
+template <int MODE>
 int bilinear_wide(int op, const float *x, const float *y, float *out, int64_t batch, int n,
                   uint32_t neg, uint32_t zero, cudaStream_t stream);
 
@@ -187,6 +190,14 @@ bool use_tiled(int op, int n, uint32_t neg, uint32_t zero, const void *x, const 
     return true;
 }
 
+// The Cl(6,1) geometric product through two Cl(6,0) sums (bilinear_tiled.cuh,
+// OPK_GP61): metric [1]*6 + [-1], the tiled kernel's alignment and size rules.
+bool use_cl61(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
+              const void *o, int64_t batch) {
+    return op == CB_OP_GP && n == 7 && neg == (1u << 6) && zero == 0 &&
+           use_tiled(op, n, neg, zero, x, y, o, batch);
+}
+
 // The large-n kernel (bilinear_wide.cuh): same sign requirements as the
 // tiled one, 11 <= n <= 16.
 bool use_wide(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
@@ -248,6 +259,13 @@ int bilinear(int op, int mode, const float *x, const float *y, float *out, int64
         return gp_mat16(mode, x, y, out, batch, stream);
     if (!direct && use_pga10(op, n, neg, zero, x, y, out))
         return pga10(mode, x, y, out, batch, stream);
+    if (!direct && use_cl61(op, n, neg, zero, x, y, out, batch)) {
+        switch (mode) {
+        case CB_MODE_FWD: return bilinear_tiled_cl61<CB_MODE_FWD>(x, y, out, batch, stream);
+        case CB_MODE_GRAD_A: return bilinear_tiled_cl61<CB_MODE_GRAD_A>(x, y, out, batch, stream);
+        default: return bilinear_tiled_cl61<CB_MODE_GRAD_B>(x, y, out, batch, stream);
+        }
+    }
     if (use_tiled(op, n, neg, zero, x, y, out, batch)) {
         switch (mode) {
         case CB_MODE_FWD:

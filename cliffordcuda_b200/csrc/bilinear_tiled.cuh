@@ -66,7 +66,7 @@ constexpr int kTileLines = kTileFloats / 32;  // 128 lines of 128 bytes
 constexpr int kTileBytes = kTileFloats * 4;
 constexpr int kStages = 2;                    // tiles in flight per CTA
 
-enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4, OPK_REG = 5 };
+enum { OPK_GP = 0, OPK_WEDGE = 1, OPK_LC = 2, OPK_RC = 3, OPK_INNER = 4, OPK_REG = 5, OPK_GP61 = 6 };
 
 __host__ __device__ constexpr int popcl(int v) {
     int c = 0;
@@ -572,6 +572,154 @@ __device__ __forceinline__ int diag_sign(int e, int kh) {
                ? -1 : 1;
 }
 
+// Cl(6,1) geometric product through Cl(6,0) + Cl(6,0) (OPK_GP61). With
+// omega = e0 ... e6 (central, omega^2 = +1) every x is u + v omega (u, v
+// even), and x -> (u + v, u - v) is an algebra isomorphism onto pairs of
+// elements of the even subalgebra, which is Cl(6,0) through f_i = e_i e_6.
+// Per Cl(6,0) blade k: f_k = a(k) e_E (E = k, plus e_6 when k is odd) and
+// e_O omega = s(O) e_(O^127), so with O = E ^ 127 and b = a s(O):
+//     P[k] = a x[E] + b x[O],  Q[k] = a x[E] - b x[O],
+// and back x[E] = a (P + Q)/2, x[O] = b (P - Q)/2. The map satisfies
+// phi^T phi = 2 I, so each of the three sums is phi^-1 of the Cl(6,0) sum of
+// the same mode over the pairs: the tile's 128-float rows turn in place into
+// pairs of 64-float rows, the n = 6 sweep runs, and the results turn back.
+// Bit k of amask / bmask: a(k) / b(k) = -1. The four lanes of a Cl(6,1) row
+// (one warp) take blades 16 l .. 16 l + 15 each.
+// In float4 chunks: with x0 / x1 the row's blades without / with e_6 and
+// chunk m = blades 4m..4m+3 (64-blade halves), E(k) = k (even parity) or
+// 64 + k (odd) and O(k) = E ^ 127 is blade 63 - k of the other half, so chunk
+// m of P and Q needs chunk m of x0, x1 and chunk 15 - m of both, reversed.
+__device__ __forceinline__ float4 ld4(const float *tile, int f) {
+    return *reinterpret_cast<const float4 *>(tile + swz_index(f));
+}
+__device__ __forceinline__ void st4(float *tile, int f, float4 v) {
+    *reinterpret_cast<float4 *>(tile + swz_index(f)) = v;
+}
+__device__ __forceinline__ float f4(const float4 &v, int j) {
+    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ float sgn_bit(uint64_t mask, int k, float v) {
+    return ((mask >> k) & 1) ? -v : v;
+}
+
+// Lane l of a row handles chunks m = 4l + c (c = 0..3), in the order
+// c ^ (2 (R & 1)) so that rows R and R + 1 of a quarter-warp touch disjoint
+// 16-byte bank groups. Its sign bits (bit i for blade k = 16 l + i): al = a(k),
+// bk = b(k), bl = b(63 - k).
+__device__ __forceinline__ void phi61_lane(int tid, uint64_t amask, uint64_t bmask, int &base,
+                                           int &l, int &cx, uint32_t &al, uint32_t &bk,
+                                           uint32_t &bl) {
+    const int R = tid >> 2;
+    l = tid & 3;
+    base = 128 * R;
+    cx = 2 * (R & 1);
+    al = (uint32_t)(amask >> (16 * l)) & 0xFFFFu;
+    bk = (uint32_t)(bmask >> (16 * l)) & 0xFFFFu;
+    const uint32_t w = (uint32_t)(bmask >> (48 - 16 * l)) & 0xFFFFu;
+    bl = __brev(w) >> 16;
+}
+
+// x rows -> [P | Q] in place, for the x and the y tile (one code copy).
+__device__ __forceinline__ void phi61_in(float *xt, float *yt, int tid, uint64_t amask,
+                                         uint64_t bmask) {
+    int base, l, cx;
+    uint32_t al, bk, bl;
+    phi61_lane(tid, amask, bmask, base, l, cx, al, bk, bl);
+#pragma unroll 1
+    for (int t = 0; t < 2; ++t) {
+        float *tile = t == 0 ? xt : yt;
+        float4 P[4], Q[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int cc = c ^ cx, m = 4 * l + cc, mr = 15 - m;
+            const float4 x0 = ld4(tile, base + 4 * m), x1 = ld4(tile, base + 64 + 4 * m);
+            const float4 r0 = ld4(tile, base + 4 * mr), r1 = ld4(tile, base + 64 + 4 * mr);
+            const int pm = parity((uint32_t)m);
+            float p[4], q[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = 4 * cc + j;                        // k = 16 l + i
+                const bool odd = pm ^ ((j ^ (j >> 1)) & 1);      // parity of k
+                const float xe = odd ? f4(x1, j) : f4(x0, j);    // x[E(k)]
+                const float xo = odd ? f4(r0, 3 - j) : f4(r1, 3 - j);  // x[O(k)]
+                const float te = ((al >> i) & 1) ? -xe : xe;
+                const float to = ((bk >> i) & 1) ? -xo : xo;
+                p[j] = te + to;
+                q[j] = te - to;
+            }
+            P[c] = make_float4(p[0], p[1], p[2], p[3]);
+            Q[c] = make_float4(q[0], q[1], q[2], q[3]);
+        }
+        __syncwarp();  // the row's four lanes have read it
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int m = 4 * l + (c ^ cx);
+            st4(tile, base + 4 * m, P[c]);
+            st4(tile, base + 64 + 4 * m, Q[c]);
+        }
+    }
+    __syncwarp();
+}
+
+// Back, in place: x0[p] = a(p) U[p] (p even parity) or b(63-p) V[63-p] (odd),
+// and x1[p] the other way round, U = (P + Q)/2, V = (P - Q)/2.
+__device__ __forceinline__ void phi61_out(float *tile, int tid, uint64_t amask, uint64_t bmask) {
+    int base, l, cx;
+    uint32_t al, bk, bl;
+    phi61_lane(tid, amask, bmask, base, l, cx, al, bk, bl);
+    float4 X0[4], X1[4];
+    __syncwarp();  // the row's lanes have stored both halves
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const int cc = c ^ cx, m = 4 * l + cc, mr = 15 - m;
+        const float4 P = ld4(tile, base + 4 * m), Q = ld4(tile, base + 64 + 4 * m);
+        const float4 Pr = ld4(tile, base + 4 * mr), Qr = ld4(tile, base + 64 + 4 * mr);
+        const int pm = parity((uint32_t)m);
+        float u0[4], u1[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = 4 * cc + j;                       // p = 16 l + i
+            const bool odd = pm ^ ((j ^ (j >> 1)) & 1);     // parity of p (= of 63 - p)
+            const float U = 0.5f * (f4(P, j) + f4(Q, j));
+            const float V = 0.5f * (f4(Pr, 3 - j) - f4(Qr, 3 - j));  // at blade 63 - p
+            const float eu = ((al >> i) & 1) ? -U : U;
+            const float ov = ((bl >> i) & 1) ? -V : V;  // b(63 - p)
+            u0[j] = odd ? ov : eu;
+            u1[j] = odd ? eu : ov;
+        }
+        X0[c] = make_float4(u0[0], u0[1], u0[2], u0[3]);
+        X1[c] = make_float4(u1[0], u1[1], u1[2], u1[3]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const int m = 4 * l + (c ^ cx);
+        st4(tile, base + 4 * m, X0[c]);
+        st4(tile, base + 64 + 4 * m, X1[c]);
+    }
+}
+
+// a / b masks of the Cl(6,1) route (metric: e6 squares to -1, e0..e5 to +1).
+inline void phi61_masks(uint64_t *amask, uint64_t *bmask) {
+    const uint32_t neg = 1u << 6;
+    *amask = *bmask = 0;
+    for (int k = 0; k < 64; ++k) {
+        uint32_t blade = 0;
+        int sign = 1;
+        for (int i = 0; i < 6; ++i) {
+            if (!((k >> i) & 1)) continue;
+            const uint32_t gs[2] = {1u << i, 1u << 6};
+            for (uint32_t g : gs) {
+                sign *= blade_sign(blade, g, neg, 0);
+                blade ^= g;
+            }
+        }
+        const int sb = sign * blade_sign(blade ^ 127u, 127u, neg, 0);
+        if (sign < 0) *amask |= 1ull << k;
+        if (sb < 0) *bmask |= 1ull << k;
+    }
+}
+
 template <int MODE, int OPK, int NEGL, bool SCHED>
 __global__ void __launch_bounds__(kThreads, 3)
     bilinear_tiled_kernel(const __grid_constant__ CUtensorMap mx,
@@ -579,7 +727,8 @@ __global__ void __launch_bounds__(kThreads, 3)
                           const __grid_constant__ CUtensorMap mo, int n, uint32_t neg,
                           uint32_t zero, int num_tiles, int *err, bool skip_zero,
                           const LowRelabel rl,
-                          const __grid_constant__ std::conditional_t<SCHED, StepSched, NoSched> sched) {
+                          const __grid_constant__ std::conditional_t<SCHED, StepSched, NoSched> sched,
+                          uint64_t phi_a, uint64_t phi_b) {
     extern __shared__ unsigned char smem_raw[];
     // 1 KB-aligned start, derived by pointer arithmetic on the shared array so
     // the compiler keeps the shared address space (32-bit LDS/STS addressing).
@@ -590,7 +739,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int NH = 1 << lgNH;
     constexpr bool inner = (OPK == OPK_INNER);
     constexpr bool reg = (OPK == OPK_REG);
-    constexpr int OPB = reg ? OPK_WEDGE : OPK;  // the sweep's product
+    constexpr bool phi = (OPK == OPK_GP61);
+    constexpr int OPB = reg ? OPK_WEDGE : (phi ? OPK_GP : OPK);  // the sweep's product
     float2 *tab = reinterpret_cast<float2 *>(ys + kStages * kTileFloats);
     float2 *tab2 = tab + NH * NH;
     uint64_t *bars = reinterpret_cast<uint64_t *>(tab + table_entries(n, inner));
@@ -658,6 +808,9 @@ __global__ void __launch_bounds__(kThreads, 3)
             relabel_line(xt, rowl + kh, rl);
             relabel_line(yt, rowl + kh, rl);
             __syncwarp();  // a row's lines are read by the row's threads, one warp
+        }
+        if constexpr (phi) {  // Cl(6,1) rows -> pairs of Cl(6,0) rows
+            phi61_in(xt, yt, tid, phi_a, phi_b);
         }
         const uint32_t allb = (uint32_t)D - 1;  // the pseudoscalar's blade
         const uint32_t dmask = (0xAAAAAAAAu ^ neg) & allb;
@@ -736,6 +889,7 @@ __global__ void __launch_bounds__(kThreads, 3)
             store_block_relabel(xt, rowl + kh, acc, rl);
         else
             store_block(xt, rowl + kh, acc);
+        if constexpr (phi) phi61_out(xt, tid, phi_a, phi_b);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -762,7 +916,8 @@ __global__ void __launch_bounds__(kThreads, 3)
 
 template <int MODE, int OPK, int NEGL>
 int launch_tiled_k(const float *x, const float *y, float *out, int64_t batch, int n, uint32_t neg,
-                   uint32_t zero, const LowRelabel &rl, cudaStream_t stream) {
+                   uint32_t zero, const LowRelabel &rl, cudaStream_t stream, uint64_t phi_a = 0,
+                   uint64_t phi_b = 0) {
     DeviceInfo di;
     int st = device_info(&di);
     if (st) return st;
@@ -794,12 +949,12 @@ int launch_tiled_k(const float *x, const float *y, float *out, int64_t batch, in
         }
         const int grid = (int)std::min<int64_t>(tiles, (int64_t)per_sm * di.sm_count);
         kern<<<grid, kThreads, smem, stream>>>(mx, my, mo, n, neg, zero, (int)tiles, err,
-                                               skip_zero, rl, sched_arg);
+                                               skip_zero, rl, sched_arg, phi_a, phi_b);
         e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(e, "launch bilinear_tiled_kernel");
         return CB_OK;
     };
-    if constexpr (OPK != OPK_GP && OPK != OPK_INNER) {
+    if constexpr (OPK != OPK_GP && OPK != OPK_INNER && OPK != OPK_GP61) {
         const StepSched sched = cached_sched(MODE, OPK, n, neg, zero);
         if (sched.T)
             return run(bilinear_tiled_kernel<MODE, OPK, NEGL, true>, smem_bytes(n, false, true),
@@ -856,6 +1011,19 @@ int bilinear_tiled(int op, const float *x, const float *y, float *out, int64_t b
     }
     set_error("op %d has no tiled kernel", op);
     return CB_ERR_INVALID;
+}
+
+// The Cl(6,1) geometric product (metric [1]*6 + [-1]) through two Cl(6,0)
+// sums per row (OPK_GP61); mode as in cb_bilinear.
+template <int MODE>
+int bilinear_tiled_cl61(const float *x, const float *y, float *out, int64_t batch,
+                        cudaStream_t stream) {
+    using namespace tiled;
+    static uint64_t amask = 0, bmask = 0;
+    static const bool once = (phi61_masks(&amask, &bmask), true);
+    (void)once;
+    return launch_tiled_k<MODE, OPK_GP61, 0>(x, y, out, 2 * batch, 6, 0, 0, make_relabel(0), stream,
+                                             amask, bmask);
 }
 
 }  // namespace cb
