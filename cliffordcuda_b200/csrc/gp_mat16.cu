@@ -342,7 +342,6 @@ __device__ __forceinline__ void quadrant_product_rt(float (&acc)[64], const floa
 // componentwise; back, u = (P + Q)/2 and v = (P - Q) w / 2, which is also the
 // adjoint map for the backward sums. Used by the Cl(9,0,1) product (pga10.cu).
 __device__ __forceinline__ float wsign9(uint32_t j) { return (__popc(j & 0xAAu) & 1) ? -1.0f : 1.0f; }
-__device__ __forceinline__ float gsign9(uint32_t j) { return (__popc(j) & 1) ? -1.0f : 1.0f; }
 
 // As gather, for component cs (+1 / -1) of the block [u | v] (optionally of
 // its grade involution, folded into S and C by the caller):
@@ -368,24 +367,24 @@ __device__ __forceinline__ void gather9(float (&r)[64], const float *u, const fl
 }
 
 struct Gp9Args {
-    const float *x, *y;  // rows of 1024 floats; blocks hx, hy
+    const float *x, *y;  // rows of 1024 floats
     float *out;          // block ho of rows of 1024 floats
-    int hx, hy, ho;
-    int gx, gy;          // use the grade involution of the x / y block
-    int gout, acc;       // grade involution of the result; add into out
+    int ho, terms;       // terms: 1 or 2 (summed in the matrix domain)
+    int hx[2], hy[2];    // per term: the x / y block
+    int gx[2], gy[2];    // per term: use the grade involution of the x / y block
 };
 
-// out_block (+)= g?(sum of mode MODE over Cl(9,0) blocks), 4 rows per warp
-// and batch: product slot p = 2 * row + component; u of a block is loaded
-// into the slot of component +, v into that of component -.
+// out_block = sum over the terms of the Cl(9,0) block sum of mode MODE, 4 rows
+// per warp and batch: product slot p = 2 * row + component; u of a block is
+// loaded into the slot of component +, v into that of component -. A second
+// term reuses the same slots: its blocks load once the first product has
+// read them, and its product adds into the first one's registers.
 template <int MODE>
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(32, 11)
     gp9_kernel(Gp9Args A, int64_t batch, int64_t nbatches, int *err) {
     constexpr bool SWAP = MODE == CB_MODE_GRAD_A;
     constexpr bool TU = MODE == CB_MODE_GRAD_B, TV = MODE == CB_MODE_GRAD_A;
     const float *gu = SWAP ? A.y : A.x, *gv = SWAP ? A.x : A.y;
-    const int hu = SWAP ? A.hy : A.hx, hv = SWAP ? A.hx : A.hy;
-    const bool giu = SWAP ? A.gy : A.gx, giv = SWAP ? A.gx : A.gy;
     extern __shared__ __align__(16) float sm[];
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + kBufFloats);
     const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
@@ -400,84 +399,92 @@ __global__ void __launch_bounds__(32)
     // Lane factors (see gp_mat16_kernel), per operand with the grade
     // involution folded in: it multiplies u[idx] by (-1)^popc(idx), whose
     // parity is popc(K) + popc(q), and turns v into -g(v), i.e. flips C.
-    float s_u[4], s_v[4], s_out[4];
+    float s_l[4], s_g[4], s_out[4];
     const int qpar = (q ^ (q >> 1)) & 1;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
         const float s = (float)last_sign(q, m);
         const float sl = q == 2 ? -s : s;
         const float gi = ((m & 1) ^ qpar) ? -1.0f : 1.0f;
-        s_u[m] = giu ? sl * gi : sl;
-        s_v[m] = giv ? sl * gi : sl;
+        s_l[m] = sl;
+        s_g[m] = sl * gi;
         s_out[m] = sl * 0.0625f;
     }
     // lane part of w(~idx): bit 1 of ~q' (q' = q, or q ^ 3 for odd K)
     const float w0 = ((q >> 1) & 1) ? 1.0f : -1.0f, w3 = ((q >> 1) & 1) ? -1.0f : 1.0f;
-    const float cu = giu ? -cs : cs, cv = giv ? -cs : cs;
     const float c_fwd = r4 ? 1.0f : -1.0f;
     const float c_inv = r4 ? -1.0f : 1.0f;
     bool ok = true;
+    int ph = 0;  // load rounds so far (mbarrier phase)
     int64_t bt = blockIdx.x;
-    for (int it = 0; bt < nbatches && ok; bt += gridDim.x, ++it) {
+    for (; bt < nbatches && ok; bt += gridDim.x) {
         const int64_t r0 = bt * 4;
         const int nv = (int)std::min<int64_t>(4, batch - r0);
-        if (lane == 0) {
-            bulk_wait_read<0>();  // the previous batch's stores have read the buffer
-            mbar_arrive_expect_tx(full, (uint32_t)nv * 4096u);
-            for (int i = 0; i < nv; ++i) {
-                const float *xu = gu + (r0 + i) * 1024 + hu * 512;
-                const float *yu = gv + (r0 + i) * 1024 + hv * 512;
-                bulk_load(sm + (2 * i) * kRowFloats, xu, 1024, full);
-                bulk_load(sm + (2 * i + 1) * kRowFloats, xu + 256, 1024, full);
-                bulk_load(sm + kRegion + (2 * i) * kRowFloats, yu, 1024, full);
-                bulk_load(sm + kRegion + (2 * i + 1) * kRowFloats, yu + 256, 1024, full);
-            }
-        }
-        ok = mbar_wait_bounded(full, it & 1, err, 0x311);
-        if (!__all_sync(0xffffffffu, ok)) break;
         float *U = sm + p * kRowFloats;
         float *V = U + kRegion;
-        float r[64];
+        float acc[64];
 #pragma unroll 1
-        for (int t = 0; t < 2; ++t) {
-            const float *raw = sm + (t == 0 ? 0 : kRegion) + (2 * prow) * kRowFloats;
-            const float c = t == 0 ? cu : cv;
-            gather9(r, raw, raw + kRowFloats, q, t == 0 ? s_u : s_v, c * w0, c * w3,
-                    std::make_integer_sequence<int, 64>{});
-            __syncwarp();  // both components of the row have read the raw block
-            to_matrix3(r);
-            factor4(r, c_fwd);
-            const bool trans = t == 0 ? TU : TV;
-            store_quadrant_rt(t == 0 ? U : V, trans ? c4 * 2 + r4 : r4 * 2 + c4, t == 0 ? !TU : TV,
-                              r);
+        for (int term = 0; term < A.terms && ok; ++term, ++ph) {
+            const int hx = term ? A.hx[1] : A.hx[0], hy = term ? A.hy[1] : A.hy[0];
+            const bool gx = term ? A.gx[1] : A.gx[0], gy = term ? A.gy[1] : A.gy[0];
+            const int hu = SWAP ? hy : hx, hv = SWAP ? hx : hy;
+            const bool giu = SWAP ? gy : gx, giv = SWAP ? gx : gy;
+            if (term > 0) fence_proxy_async_smem();  // the product's reads before the loads
+            __syncwarp();
+            if (lane == 0) {
+                if (term == 0) bulk_wait_read<0>();  // the previous batch's stores have read the buffer
+                mbar_arrive_expect_tx(full, (uint32_t)nv * 4096u);
+                for (int i = 0; i < nv; ++i) {
+                    const float *xu = gu + (r0 + i) * 1024 + hu * 512;
+                    const float *yu = gv + (r0 + i) * 1024 + hv * 512;
+                    bulk_load(sm + (2 * i) * kRowFloats, xu, 1024, full);
+                    bulk_load(sm + (2 * i + 1) * kRowFloats, xu + 256, 1024, full);
+                    bulk_load(sm + kRegion + (2 * i) * kRowFloats, yu, 1024, full);
+                    bulk_load(sm + kRegion + (2 * i + 1) * kRowFloats, yu + 256, 1024, full);
+                }
+            }
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(full, ph & 1, err, 0x311));
+            if (!ok) break;
+            float r[64];
+#pragma unroll 1
+            for (int t = 0; t < 2; ++t) {
+                const float *raw = sm + (t == 0 ? 0 : kRegion) + (2 * prow) * kRowFloats;
+                const bool gi = t == 0 ? giu : giv;
+                const float c = gi ? -cs : cs;
+                gather9(r, raw, raw + kRowFloats, q, gi ? s_g : s_l, c * w0, c * w3,
+                        std::make_integer_sequence<int, 64>{});
+                __syncwarp();  // both components of the row have read the raw block
+                to_matrix3(r);
+                factor4(r, c_fwd);
+                const bool trans = t == 0 ? TU : TV;
+                store_quadrant_rt(t == 0 ? U : V, trans ? c4 * 2 + r4 : r4 * 2 + c4,
+                                  t == 0 ? !TU : TV, r);
+            }
+            __syncwarp();
+            if (term == 0)
+                quadrant_product(acc, U, V, r4, c4);
+            else
+                quadrant_product<false, true>(acc, U, V, r4, c4);
+            __syncwarp();
         }
-        __syncwarp();
-        quadrant_product(r, U, V, r4, c4);
-        __syncwarp();
-        factor4(r, c_inv);
-        from_matrix3(r);
-        scatter(r, U, q, s_out, std::make_integer_sequence<int, 64>{});
+        if (!ok) break;
+        factor4(acc, c_inv);
+        from_matrix3(acc);
+        scatter(acc, U, q, s_out, std::make_integer_sequence<int, 64>{});
         __syncwarp();
         // merge: slot 2r holds P (component +), slot 2r + 1 holds Q; lanes 8r..8r+7
         // take the blade pairs (k, ~k), so every lane reads and writes its own places
         const int mrow = lane >> 3, j8 = lane & 7;
         if (mrow < nv) {
             float *Pz = sm + (2 * mrow) * kRowFloats, *Qz = Pz + kRowFloats;
-            const float *old = A.out + (r0 + mrow) * 1024 + A.ho * 512;
 #pragma unroll 4
             for (int t = 0; t < 16; ++t) {
                 const uint32_t k = j8 + 8 * t, nk = 255 - k;
                 const float P = Pz[k], Q = Qz[k], Pr = Pz[nk], Qr = Qz[nk];
-                float uk = 0.5f * (P + Q), unk = 0.5f * (Pr + Qr);
-                float vk = 0.5f * wsign9(nk) * (Pr - Qr), vnk = 0.5f * wsign9(k) * (P - Q);
-                if (A.gout) {  // g(u + v e8) = g(u) - g(v) e8
-                    const float gk = gsign9(k), gnk = gsign9(nk);
-                    uk *= gk; unk *= gnk; vk *= -gk; vnk *= -gnk;
-                }
-                if (A.acc) {
-                    uk += old[k]; unk += old[nk]; vk += old[256 + k]; vnk += old[256 + nk];
-                }
-                Pz[k] = uk; Pz[nk] = unk; Qz[k] = vk; Qz[nk] = vnk;
+                Pz[k] = 0.5f * (P + Q);
+                Pz[nk] = 0.5f * (Pr + Qr);
+                Qz[k] = 0.5f * wsign9(nk) * (Pr - Qr);
+                Qz[nk] = 0.5f * wsign9(k) * (P - Q);
             }
         }
         fence_proxy_async_smem();
@@ -926,11 +933,23 @@ int gp_layer_weight(const float *w, float *mats, cudaStream_t s) {
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_layer_weight_kernel");
 }
 
-// One Cl(9,0) sum of blocks (see gp9_kernel); mode as in cb_bilinear.
-int gp9(int mode, const float *x, int hx, int gx, const float *y, int hy, int gy, float *out,
-        int ho, int gout, int acc, int64_t batch, cudaStream_t s) {
-    if (batch == 0) return CB_OK;
-    const Gp9Args A{x, y, out, hx, hy, ho, gx, gy, gout, acc};
+// One Cl(9,0) sum of blocks (see gp9_kernel) into block ho of out; mode as in
+// cb_bilinear. term[t] = {hx, gx, hy, gy}: the x / y block of term t and
+// whether its grade involution is used.
+int gp9(int mode, int ho, int terms, const int (*term)[4], const float *x, const float *y,
+        float *out, int64_t batch, cudaStream_t s) {
+    Gp9Args A{};
+    A.x = x;
+    A.y = y;
+    A.out = out;
+    A.ho = ho;
+    A.terms = terms;
+    for (int t = 0; t < terms; ++t) {
+        A.hx[t] = term[t][0];
+        A.gx[t] = term[t][1];
+        A.hy[t] = term[t][2];
+        A.gy[t] = term[t][3];
+    }
     switch (mode) {
     case CB_MODE_FWD: return launch_gp9<CB_MODE_FWD>(A, batch, s);
     case CB_MODE_GRAD_A: return launch_gp9<CB_MODE_GRAD_A>(A, batch, s);

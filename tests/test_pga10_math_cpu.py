@@ -6,7 +6,9 @@ float64 with the oracle's Cl(8,0) and Cl(9,0,1) sums, no GPU:
   back by u = (P + Q)/2, v = (P - Q) w / 2 (also the adjoint the backward uses);
 * the backward sums through the same maps:
   grad_a0 = gA(b0; g0) + gA(b1; g1), grad_a1 = gA(g(b0); g1),
-  grad_b0 = gB(a0; g0) + g(gB(a1; g1)), grad_b1 = gB(a0; g1).
+  grad_b0 = gB(a0; g0) + g(gB(a1; g1)), grad_b1 = gB(a0; g1);
+* g(gB(a1; g1)) = gB(g(a1); g(g1)) (g an orthogonal automorphism), the form the
+  kernel sums in the matrix domain.
 """
 import numpy as np
 
@@ -53,3 +55,6 @@ def test_cl901_product_and_gradients_through_cl8():
     ref = O.forward_backward("gp", 10, M10, a, b, g)
     for mine, r in zip((c, ga, gb), ref):
         assert np.abs(mine - r).max() <= 1e-12 * np.abs(r).max()
+    alt = s9("grad_b", ginv9(a1), ginv9(g1))
+    ref_t = ginv9(s9("grad_b", a1, g1))
+    assert np.abs(alt - ref_t).max() <= 1e-12 * np.abs(ref_t).max()
