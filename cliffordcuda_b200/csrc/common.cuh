@@ -263,14 +263,11 @@ int gp_mat16_bwd(const float *a, const float *b, const float *g, float *ga, floa
                  int64_t batch, cudaStream_t s);
 
 // Cl(9,0,1) geometric product through Cl(8,0) matrix products (pga10.cu),
-// applicable when use_pga10 holds; gp9 writes block ho of out as the sum of
-// one or two Cl(9,0) block sums, term[t] = {hx, gx, hy, gy} (block of x, its
-// grade involution, block of y, its grade involution).
+// applicable when use_pga10 holds; pga10_sum (gp_mat16.cu) is one sum of it.
 bool use_pga10(int op, int n, uint32_t neg, uint32_t zero, const void *x, const void *y,
                const void *o);
 int pga10(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s);
-int gp9(int mode, int ho, int terms, const int (*term)[4], const float *x, const float *y,
-        float *out, int64_t batch, cudaStream_t s);
+int pga10_sum(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s);
 
 // internal bilinear dispatcher (bilinear.cu)
 // direct: always the blade-by-blade kernels (never the matrix representation).

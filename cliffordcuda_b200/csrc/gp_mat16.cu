@@ -366,27 +366,51 @@ __device__ __forceinline__ void gather9(float (&r)[64], const float *u, const fl
     (gather9_1<K>(r, u, v, q, q ^ 3, S, C0, C3), ...);
 }
 
-struct Gp9Args {
-    const float *x, *y;  // rows of 1024 floats
-    float *out;          // block ho of rows of 1024 floats
-    int ho, terms;       // terms: 1 or 2 (summed in the matrix domain)
-    int hx[2], hy[2];    // per term: the x / y block
-    int gx[2], gy[2];    // per term: use the grade involution of the x / y block
+// One whole sum of the Cl(9,0,1) product (pga10.cu) in three stages over the
+// same shared slots, 4 rows per warp and batch (product slot p = 2 * row +
+// component; u of a block loads into the slot of component +, v into that of
+// component -):
+//   stage 0: U and V load, acc = U V;
+//   stage 1: U and V load, acc += U V, then the output block h1 leaves through
+//            the V slots (U keeps its converted operand);
+//   stage 2: V loads, acc = U V, and the output block h2 leaves through U.
+// U is the A operand's tensor (y for grad_a, x otherwise), V the other one;
+// ub / vb are their blocks per stage and ug / vg whether the block's grade
+// involution is used.
+struct Pga10Plan {
+    int ub[2], ug[2];
+    int vb[3], vg[3];
+    int h1, h2;
 };
 
-// out_block = sum over the terms of the Cl(9,0) block sum of mode MODE, 4 rows
-// per warp and batch: product slot p = 2 * row + component; u of a block is
-// loaded into the slot of component +, v into that of component -. A second
-// term reuses the same slots: its blocks load once the first product has
-// read them, and its product adds into the first one's registers.
+// In place on the output slots of a region: slot 2r holds P (component +),
+// slot 2r + 1 holds Q; u = (P + Q)/2, v = (P - Q) w / 2. Lanes 8r..8r+7 take
+// the blade pairs (k, ~k), so every lane reads and writes its own places.
+__device__ __forceinline__ void merge9(float *region, int lane, int nv) {
+    const int mrow = lane >> 3, j8 = lane & 7;
+    if (mrow >= nv) return;
+    float *Pz = region + (2 * mrow) * kRowFloats, *Qz = Pz + kRowFloats;
+#pragma unroll 4
+    for (int t = 0; t < 16; ++t) {
+        const uint32_t k = j8 + 8 * t, nk = 255 - k;
+        const float P = Pz[k], Q = Qz[k], Pr = Pz[nk], Qr = Qz[nk];
+        Pz[k] = 0.5f * (P + Q);
+        Pz[nk] = 0.5f * (Pr + Qr);
+        Qz[k] = 0.5f * wsign9(nk) * (Pr - Qr);
+        Qz[nk] = 0.5f * wsign9(k) * (P - Q);
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(32, 11)
-    gp9_kernel(Gp9Args A, int64_t batch, int64_t nbatches, int *err) {
+    pga10_kernel(const float *__restrict__ x, const float *__restrict__ y, float *__restrict__ out,
+                 const Pga10Plan P, int64_t batch, int64_t nbatches, int *err) {
     constexpr bool SWAP = MODE == CB_MODE_GRAD_A;
     constexpr bool TU = MODE == CB_MODE_GRAD_B, TV = MODE == CB_MODE_GRAD_A;
-    const float *gu = SWAP ? A.y : A.x, *gv = SWAP ? A.x : A.y;
+    const float *gu = SWAP ? y : x, *gv = SWAP ? x : y;
     extern __shared__ __align__(16) float sm[];
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + kBufFloats);
+    float *const RU = sm, *const RV = sm + kRegion;
     const int lane = threadIdx.x, p = lane >> 2, q = lane & 3;
     const int r4 = q >> 1, c4 = r4 ^ (q & 1);
     const int prow = p >> 1;                         // row of this slot in the batch
@@ -414,41 +438,43 @@ __global__ void __launch_bounds__(32, 11)
     const float w0 = ((q >> 1) & 1) ? 1.0f : -1.0f, w3 = ((q >> 1) & 1) ? -1.0f : 1.0f;
     const float c_fwd = r4 ? 1.0f : -1.0f;
     const float c_inv = r4 ? -1.0f : 1.0f;
+    float *const U = RU + p * kRowFloats, *const V = RV + p * kRowFloats;
     bool ok = true;
     int ph = 0;  // load rounds so far (mbarrier phase)
-    int64_t bt = blockIdx.x;
-    for (; bt < nbatches && ok; bt += gridDim.x) {
+    for (int64_t bt = blockIdx.x; bt < nbatches && ok; bt += gridDim.x) {
         const int64_t r0 = bt * 4;
         const int nv = (int)std::min<int64_t>(4, batch - r0);
-        float *U = sm + p * kRowFloats;
-        float *V = U + kRegion;
         float acc[64];
 #pragma unroll 1
-        for (int term = 0; term < A.terms && ok; ++term, ++ph) {
-            const int hx = term ? A.hx[1] : A.hx[0], hy = term ? A.hy[1] : A.hy[0];
-            const bool gx = term ? A.gx[1] : A.gx[0], gy = term ? A.gy[1] : A.gy[0];
-            const int hu = SWAP ? hy : hx, hv = SWAP ? hx : hy;
-            const bool giu = SWAP ? gy : gx, giv = SWAP ? gx : gy;
-            if (term > 0) fence_proxy_async_smem();  // the product's reads before the loads
+        for (int st = 0; st < 3; ++st, ++ph) {
+            const bool loadU = st < 2;
+            const int hu = st == 0 ? P.ub[0] : P.ub[1];
+            const bool giu = st == 0 ? P.ug[0] : P.ug[1];
+            const int hv = st == 0 ? P.vb[0] : st == 1 ? P.vb[1] : P.vb[2];
+            const bool giv = st == 0 ? P.vg[0] : st == 1 ? P.vg[1] : P.vg[2];
+            if (st > 0) fence_proxy_async_smem();  // earlier reads of the slots before the loads
             __syncwarp();
             if (lane == 0) {
-                if (term == 0) bulk_wait_read<0>();  // the previous batch's stores have read the buffer
-                mbar_arrive_expect_tx(full, (uint32_t)nv * 4096u);
+                // stage 0: the previous batch's store from U; stage 2: this batch's from V
+                if (st != 1) bulk_wait_read<0>();
+                mbar_arrive_expect_tx(full, (uint32_t)nv * (loadU ? 4096u : 2048u));
                 for (int i = 0; i < nv; ++i) {
-                    const float *xu = gu + (r0 + i) * 1024 + hu * 512;
-                    const float *yu = gv + (r0 + i) * 1024 + hv * 512;
-                    bulk_load(sm + (2 * i) * kRowFloats, xu, 1024, full);
-                    bulk_load(sm + (2 * i + 1) * kRowFloats, xu + 256, 1024, full);
-                    bulk_load(sm + kRegion + (2 * i) * kRowFloats, yu, 1024, full);
-                    bulk_load(sm + kRegion + (2 * i + 1) * kRowFloats, yu + 256, 1024, full);
+                    if (loadU) {
+                        const float *bu = gu + (r0 + i) * 1024 + hu * 512;
+                        bulk_load(RU + (2 * i) * kRowFloats, bu, 1024, full);
+                        bulk_load(RU + (2 * i + 1) * kRowFloats, bu + 256, 1024, full);
+                    }
+                    const float *bv = gv + (r0 + i) * 1024 + hv * 512;
+                    bulk_load(RV + (2 * i) * kRowFloats, bv, 1024, full);
+                    bulk_load(RV + (2 * i + 1) * kRowFloats, bv + 256, 1024, full);
                 }
             }
             ok = __all_sync(0xffffffffu, mbar_wait_bounded(full, ph & 1, err, 0x311));
             if (!ok) break;
             float r[64];
 #pragma unroll 1
-            for (int t = 0; t < 2; ++t) {
-                const float *raw = sm + (t == 0 ? 0 : kRegion) + (2 * prow) * kRowFloats;
+            for (int t = loadU ? 0 : 1; t < 2; ++t) {
+                const float *raw = (t == 0 ? RU : RV) + (2 * prow) * kRowFloats;
                 const bool gi = t == 0 ? giu : giv;
                 const float c = gi ? -cs : cs;
                 gather9(r, raw, raw + kRowFloats, q, gi ? s_g : s_l, c * w0, c * w3,
@@ -461,56 +487,46 @@ __global__ void __launch_bounds__(32, 11)
                                   t == 0 ? !TU : TV, r);
             }
             __syncwarp();
-            if (term == 0)
-                quadrant_product(acc, U, V, r4, c4);
-            else
+            if (st == 1)
                 quadrant_product<false, true>(acc, U, V, r4, c4);
+            else
+                quadrant_product(acc, U, V, r4, c4);
             __syncwarp();
-        }
-        if (!ok) break;
-        factor4(acc, c_inv);
-        from_matrix3(acc);
-        scatter(acc, U, q, s_out, std::make_integer_sequence<int, 64>{});
-        __syncwarp();
-        // merge: slot 2r holds P (component +), slot 2r + 1 holds Q; lanes 8r..8r+7
-        // take the blade pairs (k, ~k), so every lane reads and writes its own places
-        const int mrow = lane >> 3, j8 = lane & 7;
-        if (mrow < nv) {
-            float *Pz = sm + (2 * mrow) * kRowFloats, *Qz = Pz + kRowFloats;
-#pragma unroll 4
-            for (int t = 0; t < 16; ++t) {
-                const uint32_t k = j8 + 8 * t, nk = 255 - k;
-                const float P = Pz[k], Q = Qz[k], Pr = Pz[nk], Qr = Qz[nk];
-                Pz[k] = 0.5f * (P + Q);
-                Pz[nk] = 0.5f * (Pr + Qr);
-                Qz[k] = 0.5f * wsign9(nk) * (Pr - Qr);
-                Qz[nk] = 0.5f * wsign9(k) * (P - Q);
+            if (st == 0) continue;
+            // an output block leaves: through V after stage 1, through U after stage 2
+            float *region = st == 1 ? RV : RU;
+            factor4(acc, c_inv);
+            from_matrix3(acc);
+            scatter(acc, region + p * kRowFloats, q, s_out, std::make_integer_sequence<int, 64>{});
+            __syncwarp();
+            merge9(region, lane, nv);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                const int h = st == 1 ? P.h1 : P.h2;
+                for (int i = 0; i < nv; ++i) {
+                    float *o = out + (r0 + i) * 1024 + h * 512;
+                    bulk_store(o, region + (2 * i) * kRowFloats, 1024);
+                    bulk_store(o + 256, region + (2 * i + 1) * kRowFloats, 1024);
+                }
+                bulk_commit();
             }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-            for (int i = 0; i < nv; ++i) {
-                float *o = A.out + (r0 + i) * 1024 + A.ho * 512;
-                bulk_store(o, sm + (2 * i) * kRowFloats, 1024);
-                bulk_store(o + 256, sm + (2 * i + 1) * kRowFloats, 1024);
-            }
-            bulk_commit();
         }
     }
     if (lane == 0) bulk_wait_all();
 }
 
 template <int MODE>
-int launch_gp9(const Gp9Args &A, int64_t batch, cudaStream_t s) {
+int launch_pga10(const float *x, const float *y, float *out, const Pga10Plan &P, int64_t batch,
+                 cudaStream_t s) {
     DeviceInfo di;
     int st = device_info(&di);
     if (st) return st;
     int *err = nullptr;
     if ((st = device_error_word(&err))) return st;
-    auto kern = gp9_kernel<MODE>;
+    auto kern = pga10_kernel<MODE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gp9)");
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pga10)");
     int ps = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, kern, 32, kSmemBytes) != cudaSuccess ||
         ps < 1) {
@@ -519,9 +535,9 @@ int launch_gp9(const Gp9Args &A, int64_t batch, cudaStream_t s) {
     }
     const int64_t nb = (batch + 3) / 4;
     const int grid = (int)std::min<int64_t>(nb, (int64_t)ps * di.sm_count);
-    kern<<<grid, 32, kSmemBytes, s>>>(A, batch, nb, err);
+    kern<<<grid, 32, kSmemBytes, s>>>(x, y, out, P, batch, nb, err);
     e = cudaGetLastError();
-    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp9_kernel");
+    return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch pga10_kernel");
 }
 
 // Both backward sums in one pass over a, b, g (5 KB per product instead of 6 KB
@@ -933,27 +949,26 @@ int gp_layer_weight(const float *w, float *mats, cudaStream_t s) {
     return e == cudaSuccess ? CB_OK : cuda_fail(e, "launch gp_layer_weight_kernel");
 }
 
-// One Cl(9,0) sum of blocks (see gp9_kernel) into block ho of out; mode as in
-// cb_bilinear. term[t] = {hx, gx, hy, gy}: the x / y block of term t and
-// whether its grade involution is used.
-int gp9(int mode, int ho, int terms, const int (*term)[4], const float *x, const float *y,
-        float *out, int64_t batch, cudaStream_t s) {
-    Gp9Args A{};
-    A.x = x;
-    A.y = y;
-    A.out = out;
-    A.ho = ho;
-    A.terms = terms;
-    for (int t = 0; t < terms; ++t) {
-        A.hx[t] = term[t][0];
-        A.gx[t] = term[t][1];
-        A.hy[t] = term[t][2];
-        A.gy[t] = term[t][3];
-    }
+// One sum of the Cl(9,0,1) product (see pga10_kernel); mode and (x, y) as in
+// cb_bilinear. The stage plans (blocks and involutions per stage, output
+// blocks): forward (x = a, y = b) c1 = a1 g(b0) + a0 b1, then c0 = a0 b0;
+// grad_a (x = b, y = g; U = g) ga0 = gA(b0; g0) + gA(b1; g1), then
+// ga1 = gA(g(b0); g1); grad_b (x = a, y = g; U = a) gb0 = gB(g(a1); g(g1)) +
+// gB(a0; g0), then gb1 = gB(a0; g1).
+int pga10_sum(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s) {
     switch (mode) {
-    case CB_MODE_FWD: return launch_gp9<CB_MODE_FWD>(A, batch, s);
-    case CB_MODE_GRAD_A: return launch_gp9<CB_MODE_GRAD_A>(A, batch, s);
-    default: return launch_gp9<CB_MODE_GRAD_B>(A, batch, s);
+    case CB_MODE_FWD: {
+        const Pga10Plan P{{1, 0}, {0, 0}, {0, 1, 0}, {1, 0, 0}, 1, 0};
+        return launch_pga10<CB_MODE_FWD>(x, y, out, P, batch, s);
+    }
+    case CB_MODE_GRAD_A: {
+        const Pga10Plan P{{0, 1}, {0, 0}, {0, 1, 0}, {0, 0, 1}, 0, 1};
+        return launch_pga10<CB_MODE_GRAD_A>(x, y, out, P, batch, s);
+    }
+    default: {
+        const Pga10Plan P{{1, 0}, {1, 0}, {1, 0, 1}, {1, 0, 0}, 0, 1};
+        return launch_pga10<CB_MODE_GRAD_B>(x, y, out, P, batch, s);
+    }
     }
 }
 

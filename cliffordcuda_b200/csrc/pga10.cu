@@ -14,10 +14,10 @@
 //     componentwise. Its inverse is u = (X+ + X-)/2, v = (X+ - X-) w / 2,
 //     and g(x) maps to (g(X-), g(X+)).
 // So a sum is three Cl(9,0) sums of blocks, each two Cl(8,0) 16 x 16 x 16
-// matrix products (gp9_kernel in gp_mat16.cu: the split into components in
+// matrix products (pga10_kernel in gp_mat16.cu: the split into components in
 // its gather, the merge in its epilogue), instead of the 4^10 blade terms of
-// the direct sum; the two sums that share an output block run in one kernel. The backward sums follow by the chain rule
-// through the same linear maps (the adjoint of x -> (X+, X-) is
+// the direct sum; one launch runs the three of a sum. The backward sums follow
+// by the chain rule through the same linear maps (the adjoint of x -> (X+, X-) is
 // (P, Q) -> [P + Q | (P - Q) w]; g and right multiplication by w are
 // orthogonal and their own adjoints):
 //   grad_a0 = gA(b0; g0) + gA(b1; g1), grad_a1 = gA(g(b0); g1),
@@ -34,32 +34,13 @@ bool use_pga10(int op, int n, uint32_t neg, uint32_t zero, const void *x, const 
     return op == CB_OP_GP && n == 10 && neg == 0 && zero == (1u << 9) && al(x) && al(y) && al(o);
 }
 
-// One sum of the Cl(9,0,1) product; mode and (x, y) as in cb_bilinear. Each
-// output block is one gp9 call; the two-term ones sum in the matrix domain.
-// The second term of grad_b0 uses g(gB(a1; g1)) = gB(g(a1); g(g1)) (g is an
-// automorphism and orthogonal), so no involution of a result is needed.
+// One sum of the Cl(9,0,1) product; mode and (x, y) as in cb_bilinear: one
+// launch of pga10_kernel (gp_mat16.cu), whose three stages compute the three
+// block sums (the two that share an output block summed in the matrix domain;
+// grad_b0's second term as g(gB(a1; g1)) = gB(g(a1); g(g1)), g being an
+// orthogonal automorphism).
 int pga10(int mode, const float *x, const float *y, float *out, int64_t batch, cudaStream_t s) {
-    int st;
-    switch (mode) {
-    case CB_MODE_FWD: {  // x = a, y = b: c0 = a0 b0, c1 = a0 b1 + a1 g(b0)
-        const int t0[1][4] = {{0, 0, 0, 0}};
-        const int t1[2][4] = {{0, 0, 1, 0}, {1, 0, 0, 1}};
-        if ((st = gp9(mode, 0, 1, t0, x, y, out, batch, s))) return st;
-        return gp9(mode, 1, 2, t1, x, y, out, batch, s);
-    }
-    case CB_MODE_GRAD_A: {  // x = b, y = g
-        const int t0[2][4] = {{0, 0, 0, 0}, {1, 0, 1, 0}};
-        const int t1[1][4] = {{0, 1, 1, 0}};
-        if ((st = gp9(mode, 0, 2, t0, x, y, out, batch, s))) return st;
-        return gp9(mode, 1, 1, t1, x, y, out, batch, s);
-    }
-    default: {  // GRAD_B: x = a, y = g
-        const int t0[2][4] = {{0, 0, 0, 0}, {1, 1, 1, 1}};
-        const int t1[1][4] = {{0, 0, 1, 0}};
-        if ((st = gp9(mode, 0, 2, t0, x, y, out, batch, s))) return st;
-        return gp9(mode, 1, 1, t1, x, y, out, batch, s);
-    }
-    }
+    return pga10_sum(mode, x, y, out, batch, s);
 }
 
 }  // namespace cb
