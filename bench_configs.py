@@ -318,7 +318,7 @@ def pga(args, world, rank, dev, T):
         flops = 3 * 2 * nnz_table(op, n, metric) * B
         bytes_ = 8 * D * 4 * B  # forward: a, b, c; backward: a, b, g, grad_a, grad_b
         res[op] = {"route": "dual numbers over Cl(9,0) = Cl(8,0) + Cl(8,0): six 16x16 matrix "
-                            "products per sum (gp9_kernel)" if op == "gp" else
+                            "products per sum, one launch (pga10_kernel)" if op == "gp" else
                             "tiled blade-by-blade kernel",
                    "products_per_s": world * B / (ms / 1e3), "ms_per_step": ms,
                    "fp32_tflops": flops / (ms / 1e3) / 1e12,
