@@ -20,9 +20,10 @@
 // register blocks: a thread owns the 32 outputs of one high block k_h of one
 // row and sweeps the high blocks i_h, each step doing up to 1024 FFMAs of
 //     acc[k_l] += c(i_l, k_l) * x[i_h, i_l] * y'[i_h ^ k_h, i_l ^ k_l]
-// whose coefficients c in {-1, 0, +1} are compile-time constants (this needs
-// the low five generators to square to +1; other metrics take the generic
-// kernel). The runtime high-part sign and predicate are folded into y' (32
+// whose coefficients c in {-1, 0, +1} are compile-time constants (one body per
+// count of low generators squaring to -1, which a runtime relabelling moves
+// to the top of the low block; null low generators take the generic kernel).
+// The runtime high-part sign and predicate are folded into y' (32
 // FMULs per step, read from a per-CTA table), and so is the y side of the
 // (-1)^(popc * popc) cross term, which depends only on the parity of y's low
 // index once the step is fixed. What remains of the cross term is a sign on
@@ -38,13 +39,16 @@
 // stage; the last warp to finish issues the TMA store of the tile and the
 // next load into the stage. No warp waits on another except through the
 // pipeline (no CTA-wide barrier in the loop, no polling producer warp); the
-// inner product's diagonal correction is a warp-shuffle reduction. A 32-float block is one 128-byte
-// line, and the swizzle makes the XOR-indexed line reads of y (eight lanes
-// of a quarter-warp on eight different lines) conflict-free.
+// inner product's diagonal correction is a warp-shuffle reduction. A 32-float
+// block is one 128-byte line, and the swizzle makes the XOR-indexed line reads
+// of y (eight lanes of a quarter-warp on eight different lines) conflict-free.
 //
 // The inner product's predicate (P subset Q or Q subset P) does not factor;
 // it is evaluated as left + right contraction minus the doubly counted
-// P == Q terms.
+// P == Q terms. The sparse products (wedge, contractions, regressive) can run
+// under a balanced step schedule (StepSched), and the Cl(6,1) geometric
+// product runs as two Cl(6,0) sums per row (OPK_GP61); both are described
+// where they are defined below.
 #pragma once
 #include <algorithm>
 #include <map>
