@@ -46,7 +46,15 @@ namespace {
 
 using namespace mat16;
 
-constexpr int kRowFloats = 292;
+// Shared layout of one product's row region: the raw 256-float row, then in
+// place the four 8 x 8 quadrant blocks at a 72-float stride (their 16-byte
+// chunks fall on bank groups 0, 2, 4, 6 mod 8). The region is 284 floats (71
+// chunks, odd): the next product's blocks take bank groups 1, 3, 5, 7, so a
+// quarter-warp's float4 block accesses (two products, four lanes each) are
+// conflict-free, and the scalar gather of 8 products spreads over all 32 banks.
+// 284 = 3 * 72 + 64 (the last block needs no padding) keeps a warp at 18.2 KB:
+// 12 one-warp CTAs per SM.
+constexpr int kRowFloats = 284;
 constexpr int kBlockFloats = 72;
 constexpr int kRegion = 8 * kRowFloats;      // 8 products
 constexpr int kBufFloats = 2 * kRegion;      // U and V
@@ -224,7 +232,7 @@ __device__ __forceinline__ void store_quadrant_rt(float *mat, int blk, bool j_ma
 // out = rho^-1(op(U) op(V)): FWD U = x, V = y; GRAD_A (x = b, y = g) U = g,
 // V = b transposed; GRAD_B (x = a, y = g) U = a transposed, V = g.
 // One buffer per warp; the load latency of one warp's batch is hidden by the
-// other warps of the SM (11 per SM; a second, prefetching buffer per warp
+// other warps of the SM (12 per SM; a second, prefetching buffer per warp
 // halves that count and measured 20% slower).
 template <int MODE>
 __global__ void __launch_bounds__(32)
@@ -402,7 +410,7 @@ __device__ __forceinline__ void merge9(float *region, int lane, int nv) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(32, 11)
+__global__ void __launch_bounds__(32, 12)
     pga10_kernel(const float *__restrict__ x, const float *__restrict__ y, float *__restrict__ out,
                  const Pga10Plan P, int64_t batch, int64_t nbatches, int *err) {
     constexpr bool SWAP = MODE == CB_MODE_GRAD_A;
@@ -550,7 +558,7 @@ int launch_pga10(const float *x, const float *y, float *out, const Pga10Plan &P,
 // The phases and their input conversions are loops, not unrolled copies: the
 // eleven warps of an SM run at different points of the kernel, and one copy
 // of each piece keeps the instruction working set small. Two regions per
-// product: 11 CTAs per SM (against 8 with all three rows resident).
+// product: 12 CTAs per SM (against 8 with all three rows resident).
 __global__ void __launch_bounds__(32)
     gp_mat16_bwd_kernel(const float *__restrict__ a, const float *__restrict__ b,
                         const float *__restrict__ g, float *__restrict__ ga,
