@@ -39,10 +39,10 @@ FLOPS_PER_SUM = 2 * NNZ_GP            # one FMA per non-zero term
 BYTES_PER_SUM = 3 * D * 4             # two operand rows read, one row written
 BYTES_PER_BWD = 5 * D * 4             # a, b, g read; grad_a, grad_b written
 # DRAM bytes per row of one gp_mat16_bwd_kernel launch, from ncu: dram__bytes_read.sum
-# + dram__bytes_write.sum of a 262,144-row launch / rows ((805.3 + 498.3) MB / 262,144).
+# + dram__bytes_write.sum of a 262,144-row launch / rows ((805.3 + 494.6) MB / 262,144).
 # Every row is read once and written once, so the per-launch traffic is this
 # times the batch.
-MEASURED_TRAFFIC_PER_BWD = (805.3e6 + 498.3e6) / 262144
+MEASURED_TRAFFIC_PER_BWD = (805.3e6 + 494.6e6) / 262144
 
 
 def hbm_peak_gbs():
