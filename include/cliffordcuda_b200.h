@@ -71,13 +71,15 @@ CB_API int cb_bilinear(int op, int mode, const float *x, const float *y, float *
 /*
  * As cb_bilinear, always through the blade-by-blade sum kernels: the sum
  * out[i ^ j] += s(i, j) x_i y_j evaluated term by term on the CUDA cores.
- * cb_bilinear takes faster routes for two geometric products: Euclidean
- * Cl(8,0) through its real 16 x 16 matrix representation, and Cl(9,0,1)
+ * cb_bilinear takes faster routes for three geometric products: Euclidean
+ * Cl(8,0) through its real 16 x 16 matrix representation; Cl(9,0,1)
  * (e0..e8 square to +1, e9 to 0) as dual numbers over Cl(9,0) =
- * Cl(8,0) + Cl(8,0), six 16 x 16 products per sum (same results to fp32
- * rounding); this entry point keeps the term-by-term kernels reachable, for
- * comparison and for callers that want them. Same reference interface as
- * cb_bilinear (extensions/ga/geom_prod.py:216-250 and its siblings).
+ * Cl(8,0) + Cl(8,0), six 16 x 16 products per sum; and Cl(6,1) (e6 squares
+ * to -1) as two Cl(6,0) sums through its central pseudoscalar (same results
+ * to fp32 rounding). This entry point keeps the term-by-term kernels
+ * reachable, for comparison and for callers that want them. Same reference
+ * interface as cb_bilinear (extensions/ga/geom_prod.py:216-250 and its
+ * siblings).
  */
 CB_API int cb_bilinear_direct(int op, int mode, const float *x, const float *y, float *out,
                               int64_t batch, int n, uint32_t neg_mask, uint32_t zero_mask,
