@@ -260,12 +260,13 @@ def test_pga10_route(batch):
     assert rel_l2(got[0], d.cpu().numpy()) < 1e-6
 
 
-@pytest.mark.parametrize("op", ["wedge", "lc", "rc", "reg"])
+@pytest.mark.parametrize("op", ["wedge", "lc", "rc", "reg", "inner"])
 @pytest.mark.parametrize("n,top", [(9, (0,)), (10, (0, 0)), (10, (-1,)), (8, (0, -1))])
 def test_balanced_step_schedule(op, n, top):
     """The sparse products at n = 8..10 run under the balanced step schedule
     (heavy output blocks lend step segments to light lanes; the lent sums come
-    back through the row's y lines): null high generators change the per-block
+    back through the row's y lines), the inner product under its two-phase
+    form (LC rounds, then RC rounds): null high generators change the per-block
     step counts, and every mode has its own pattern."""
     if op == "reg" and 0 in top:
         top = tuple(-1 if v == 0 else v for v in top)
