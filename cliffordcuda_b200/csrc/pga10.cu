@@ -1,6 +1,6 @@
 // pga10.cu -- the geometric product of Cl(9,0,1) (nine generators squaring to
-// +1, the tenth, e9, to 0: BASELINE config 5's algebra) through Cl(8,0)
-// matrix products.
+// +1, the tenth, e9, to 0: the projective algebra of the Cl(9,0,1) benchmark
+// configuration) through Cl(8,0) matrix products.
 //
 // Two exact algebra maps reduce it to the Cl(8,0) product of gp_mat16.cu:
 //   * dual numbers: with a = a0 + a1 e9 (a0, a1 in Cl(9,0); rows split as
