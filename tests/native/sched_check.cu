@@ -2,7 +2,8 @@
 // for every n = 5..10, mode and a few metrics, each step with a non-zero
 // high-part factor is scheduled exactly once, to the right output line, no
 // lane runs more than the schedule's round count, and the donor masks match
-// the borrowed segments. Prints "bad <count>" and the schedules' lengths.
+// the borrowed segments. Prints "bad <count>", the schedules' lengths and the
+// sign masks of the Cl(6,1) route.
 #include <cstdio>
 
 #include "../../cliffordcuda_b200/csrc/bilinear_tiled.cuh"
@@ -65,6 +66,10 @@ int main() {
         const StepSched s = make_sched(mode, OPK_LC, 10, 0, 1u << 9);
         printf("lc10 mode %d rounds %d\n", mode, s.T);
     }
+    // the Cl(6,1) route's sign masks (a(k), b(k) = -1 for bit k set)
+    uint64_t am = 0, bm = 0;
+    phi61_masks(&am, &bm);
+    printf("phi61 %016llx %016llx\n", (unsigned long long)am, (unsigned long long)bm);
     printf("active %d inner %d\nbad %d\n", active, iactive, bad);
     return 0;
 }

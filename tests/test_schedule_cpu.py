@@ -4,7 +4,8 @@ non-zero high-part factor is scheduled exactly once and to the right line,
 that no lane exceeds the round count, and that the donor masks match the
 borrowed segments, for n = 5..10, every sum and null high generators; and
 that the config-5 left contraction gets six rounds per sum (16 and 32 on the
-row-major sweep)."""
+row-major sweep); and that the Cl(6,1) route's sign masks equal the tables of
+tests/test_cl61_math_cpu.py, which are checked there against the oracle."""
 import os
 import shutil
 import subprocess
@@ -26,6 +27,11 @@ def test_step_schedules(tmp_path):
     assert "bad 0" in out, out
     for mode in range(3):
         assert f"lc10 mode {mode} rounds 6" in out, out
+    from tests.test_cl61_math_cpu import tables
+    _, A, B = tables()
+    am = sum(1 << k for k in range(64) if A[k] < 0)
+    bm = sum(1 << k for k in range(64) if B[k] < 0)
+    assert f"phi61 {am:016x} {bm:016x}" in out, out
     active = int(out.split("active ")[1].split()[0])
     inner = int(out.split("inner ")[1].split()[0])
     assert active > 0 and inner > 0, out
